@@ -1,0 +1,329 @@
+"""Benchmark of the submanifold-conv path: kernel-map build + implicit-GEMM conv.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cube] [--impl ours|reference]
+
+One step = ``sparse_submanifold_conv3d(feats, coords, shape, weight, IMPLICIT_GEMM)`` on one
+batch with no cached map: hash-table build, kernel map, voxel order and conv. The default
+workload is the random-occupancy cube (B=4, 128^3, p=0.02, C=32 -> 32, 3^3, fp16); other
+workloads (``indoor``, ``lidar``, ``wide3``, ``wide5``, ``toy``) run with ``--workload``.
+
+Metric: voxels/s over all ranks (plus effective TFLOP/s in ``effective``). Under torchrun
+each rank runs its own batch of the same shape (seed = rank): weak scaling, no collective
+on the data path; the step time is the max over ranks of the summed per-step CUDA-event
+durations. The L2 (126 MB) is flushed by a 256 MB write between timed steps, outside the
+step events.
+
+``e2e`` is the same metric through the public API from pinned host buffers: H2D copy of
+coords and features, the op, D2H copy of the output, all inside the timed region.
+
+``--impl reference`` times the reference's CPU path on this host instead: the oracle's C
+restatement of the reference map builder (OpenMP, all cores) plus the reference's
+EXPLICIT_GEMM forward restated on CPU torch in fp32 (all threads); rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sparse-conv_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "subm-conv3d voxels/sec (map build + conv)"
+UNIT = "voxels/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _alg_figures(w, nnz: int):
+    Ci, Co = int(w.weight.shape[-1]), int(w.weight.shape[0])
+    V = w.kernel_volume
+    M = w.num_voxels
+    s = torch.tensor([], dtype=w.dtype).element_size()
+    MW = (V + 31) // 32
+    flops_alg = 2.0 * Ci * Co * nnz
+    flops_dense = 2.0 * Ci * Co * M * V
+    # algorithmic bytes per launch (each distinct row counted once)
+    conv_bytes = M * (Ci * s + Co * s + 4 * V + 4 * MW + 4) + Co * V * Ci * s
+    map_bytes = M * (16 + 4 * V + 4 * MW)              # map_kernel: coords in, map + masks out
+    insert_bytes = M * (16 + 8)                          # coords in, one table slot written
+    order_bytes = M * (4 * MW + 4)
+    return dict(flops_alg=flops_alg, flops_dense=flops_dense, conv_bytes=conv_bytes,
+                map_bytes=map_bytes, insert_bytes=insert_bytes, order_bytes=order_bytes)
+
+
+def run_reference(args):
+    world, rank, _local = _dist()
+    if rank != 0:
+        return 0
+    sys.path.insert(0, ROOT)
+    from oracle import oracle
+    from sparseconv import synthetic
+    w = synthetic.make(args.workload, seed=0)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    feats32 = w.feats.float()
+    weight32 = w.weight.float()
+
+    def step():
+        nbr = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation, nthreads=cores)
+        return oracle.explicit_gemm_cpu(feats32, nbr, weight32)
+
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    total = float(np.sum(times))
+    value = w.num_voxels * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": dict(w.describe(), l2="n/a (host CPU)"),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"the full {w.name} workload ({w.num_voxels} voxels) per step: "
+                                   "oracle C map build (OpenMP) + EXPLICIT_GEMM restated on CPU torch fp32"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline(w, budget_s: float = 10.0):
+    sys.path.insert(0, ROOT)
+    from oracle import oracle
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    feats32, weight32 = w.feats.float(), w.weight.float()
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        nbr = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation, nthreads=cores)
+        oracle.explicit_gemm_cpu(feats32, nbr, weight32)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s or len(times) >= 20:
+            break
+    t = float(np.median(times))
+    return {"value": w.num_voxels / t, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"full {w.name} workload ({w.num_voxels} voxels), median of {len(times)} runs: "
+                      "oracle C map build (OpenMP) + EXPLICIT_GEMM restated on CPU torch fp32"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="cube")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+        pg = torch.distributed.group.WORLD
+
+    from sparseconv import _native, synthetic
+    from sparseconv.ops.submanifold_conv3d import Algorithm, sparse_submanifold_conv3d
+
+    w = synthetic.make(args.workload, seed=rank)
+    coords_h = torch.from_numpy(w.coords).pin_memory()
+    feats_h = w.feats.pin_memory()
+    coords = coords_h.to(dev)
+    feats = feats_h.to(dev)
+    weight = w.weight.to(dev)
+    shape = torch.Size(w.shape)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+
+    def step():
+        return sparse_submanifold_conv3d(feats, coords, shape, weight, algorithm=Algorithm.IMPLICIT_GEMM)
+
+    for _ in range(args.warmup):
+        out, cache = step()
+    torch.cuda.synchronize()
+    _native.check_errors(dev)
+    nnz = int((cache.neighbor_map.view(torch.int32) >= 0).sum().item())
+    fig = _alg_figures(w, nnz)
+
+    # ---------------- device-resident timed region ----------------
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    _native.stage_timing(K)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if pg is not None:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    for i in range(K):
+        flush.fill_(i)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    stage = _native.stage_times_ms()
+    _native.stage_timing(0)
+    _native.check_errors(dev)
+    step_ms = float(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
+    t = torch.tensor([step_ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    max_ms = float(t.item())
+    total_voxels = torch.tensor([w.num_voxels], dtype=torch.float64, device=dev)
+    if pg is not None:
+        torch.distributed.all_reduce(total_voxels)
+    voxels_all = float(total_voxels.item())
+    value = voxels_all * K / (max_ms / 1e3)
+
+    # ---------------- end-to-end through the public API from host buffers ----------------
+    KE = args.e2e_steps or max(3, min(K, 50))
+    out_h = torch.empty((w.num_voxels, int(w.weight.shape[0])), dtype=w.dtype).pin_memory()
+    if pg is not None:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(KE):
+        c_d = coords_h.to(dev, non_blocking=True)
+        f_d = feats_h.to(dev, non_blocking=True)
+        o, _c = sparse_submanifold_conv3d(f_d, c_d, shape, weight, algorithm=Algorithm.IMPLICIT_GEMM)
+        out_h.copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if pg is not None:
+        torch.distributed.all_reduce(e2e_ms, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = voxels_all * KE / (float(e2e_ms.item()) / 1e3)
+    _native.check_errors(dev)
+
+    if rank == 0:
+        hbm, tc, peak_kind = _peaks()
+        # dominant kernel by live stage time
+        per_stage = {k: v for k, v in stage.items() if v[1] > 0}
+        kern_bytes = {"conv": fig["conv_bytes"], "map": fig["map_bytes"],
+                      "insert": fig["insert_bytes"], "order": fig["order_bytes"]}
+        dom = max((k for k in per_stage if k in kern_bytes), key=lambda k: per_stage[k][0])
+        dom_ms = per_stage[dom][0] / per_stage[dom][1]
+        achieved = kern_bytes[dom] / (dom_ms / 1e3) / 1e9
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get(f"{args.workload}:{dom}")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": max_ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": str(w.dtype).replace("torch.", "").replace("float16", "f16").replace("bfloat16", "bf16").replace("float32", "f32"),
+            "data": "synthetic",
+            "config": dict(w.describe(), per_rank=True, l2="flushed between steps (256 MB write)",
+                           nnz_per_voxel=nnz / w.num_voxels, parallelism=f"batch-sharded x{world}"),
+            "effective": {"tflops_alg": fig["flops_alg"] * world * K / (max_ms / 1e3) / 1e12,
+                          "tflops_dense_equivalent": fig["flops_dense"] * world * K / (max_ms / 1e3) / 1e12},
+            "stages_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in per_stage.items()},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
+                         "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
+                         "algorithmic_bytes": kern_bytes[dom], "traffic": traffic},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": int(coords_h.numel() * 4 + feats_h.numel() * feats_h.element_size()),
+                    "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()), "steps": KE},
+            "gpu_launches": 4 * K,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w)
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,145 @@
+/*
+ * sparseconv_b200 -- C ABI of the B200 (sm_100a) submanifold 3D sparse-convolution library.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*,
+ * NULL = legacy default stream), launches asynchronously on that stream, and returns an
+ * SPCONV_* code. Host-side validation failures return SPCONV_ERR_ARG; a failed CUDA launch
+ * returns SPCONV_ERR_CUDA; in both cases spconv_last_error() holds a message (per thread).
+ * Problems found on the device (coordinates out of range, a full hash table, duplicate
+ * coordinates, a spin-wait limit reached) are OR-ed as SPCONV_STATUS_* bits into the
+ * caller's int32 `status` word in device memory; the caller reads it when it next syncs.
+ *
+ * Reference interfaces replaced (paths inside Arktetra/sparse-conv):
+ *   - spconv_hashmap_capacity / spconv_neighbor_map_workspace_bytes
+ *       replace the table allocation policy of src/sparseconv/ops/utils.py:3-16
+ *       (init_hashmap) and ops/submanifold_conv3d.py:43-45 (capacity = 2.0 * M).
+ *   - spconv_build_submanifold_neighbor_map
+ *       replaces hashmap_build_submanifold_conv_neighbor_map_cuda_naive,
+ *       src/sparseconv/kernels/cuda/neighbor_map/neighbor_map.h:16-28
+ *       (implementation neighbor_map.cu:179-237, bound in kernels/cuda/ext.cpp:9).
+ *   - spconv_submanifold_conv_forward
+ *       replaces sparse_submanifold_conv_fwd_implicit_gemm,
+ *       src/sparseconv/kernels/triton/implicit_gemm.py:59-86, and the EXPLICIT_GEMM
+ *       forward of ops/submanifold_conv3d.py:76-86.
+ */
+#ifndef SPARSECONV_B200_H
+#define SPARSECONV_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes. */
+#define SPCONV_OK 0
+#define SPCONV_ERR_ARG 1
+#define SPCONV_ERR_CUDA 2
+#define SPCONV_ERR_UNSUPPORTED 3
+
+/* Device status bits (OR-ed into *status by kernels). */
+#define SPCONV_STATUS_COORD_RANGE 1   /* a coordinate lies outside [0,N)x[0,W)x[0,H)x[0,D) */
+#define SPCONV_STATUS_TABLE_FULL 2    /* a probe sequence visited every slot */
+#define SPCONV_STATUS_DUPLICATE 4     /* a coordinate occurs twice; the highest row is kept */
+#define SPCONV_STATUS_WAIT_TIMEOUT 8  /* a kernel-internal wait hit its time limit */
+
+/* Feature dtypes. */
+#define SPCONV_F32 0
+#define SPCONV_F16 1
+#define SPCONV_BF16 2
+
+/* Conv kernel selection for spconv_submanifold_conv_forward_ex. */
+#define SPCONV_KERNEL_AUTO 0
+#define SPCONV_KERNEL_SIMT 1      /* CUDA-core FMA kernel, any channel count, fp32 exact path */
+#define SPCONV_KERNEL_TCGEN05 2   /* tcgen05/TMEM tensor-core kernel, fp16/bf16, C in {16,32,64,128} */
+
+/* ABI version of this header. */
+#define SPCONV_ABI_VERSION 1
+
+int spconv_abi_version(void);
+
+/* Message of the last host-side error on the calling thread ("" if none). */
+const char *spconv_last_error(void);
+
+/* Slots of the coordinate hash table for num_coords voxels: the next power of two
+ * >= 2 * num_coords (at least 1024), so the load factor stays in (0.25, 0.5].
+ * Replaces the sizing of ops/utils.py:3-16 + ops/submanifold_conv3d.py:43-45. */
+int64_t spconv_hashmap_capacity(int64_t num_coords);
+
+/* Number of uint32 words of the per-voxel offset mask: ceil(kernel_volume / 32). */
+int spconv_mask_words(int kernel_volume);
+
+/* Device workspace (bytes) that spconv_build_submanifold_neighbor_map needs for
+ * num_coords voxels on a grid of batch*W*H*D cells. 256-byte alignment suffices. */
+int64_t spconv_neighbor_map_workspace_bytes(int64_t num_coords, int batch, int W, int H, int D);
+
+/* Build the submanifold kernel map of num_coords voxels.
+ *   coords       [M,4] int32 (b,x,y,z), device, 16-byte aligned
+ *   batch,W,H,D  the NCWHD sizes without C (ops/submanifold_conv3d.py:41)
+ *   Kw,Kh,Kd     kernel size; Dw,Dh,Dd dilation
+ *   workspace    >= spconv_neighbor_map_workspace_bytes(...) bytes of device memory;
+ *                its contents on entry do not matter (the call clears what it uses)
+ *   neighbor_map [M,V] int32 output, V = Kw*Kh*Kd, row-major in the reference's offset
+ *                order (v = ((dx*Kh)+dy)*Kd+dz); -1 (0xFFFFFFFF) for a missing neighbour;
+ *                entry v == V/2 is the voxel's own row. Bit-identical to the reference's
+ *                uint32 map (neighbor_map.cu:145-176).
+ *   masks        [M, spconv_mask_words(V)] uint32 output: bit v set iff neighbor_map[i,v] >= 0
+ *   order        [M] int32 output: a permutation of 0..M-1 that groups voxels with equal
+ *                popcount and similar masks (the conv kernels' tile order). Its order within
+ *                a group is unspecified; conv results do not depend on it.
+ *   status       device int32, OR-ed with SPCONV_STATUS_* bits
+ * Replaces neighbor_map.h:16-28 (hashmap_build_submanifold_conv_neighbor_map_cuda_naive). */
+int spconv_build_submanifold_neighbor_map(
+    const int32_t *coords, int64_t num_coords,
+    int batch, int W, int H, int D,
+    int Kw, int Kh, int Kd, int Dw, int Dh, int Dd,
+    void *workspace, int64_t workspace_bytes,
+    int32_t *neighbor_map, uint32_t *masks, int32_t *order,
+    int32_t *status, void *stream);
+
+/* Submanifold conv forward over a kernel map:
+ *   out[i, co] = bias[co] + sum_v sum_ci feats[nbr[i,v], ci] * weight[co, v, ci]
+ * with fp32 accumulation, rounded once to `dtype` (no atomics, each output row written once).
+ *   feats   [M, Ci] in dtype; weight [Co, V, Ci] (= [Co,Kw,Kh,Kd,Ci]) in dtype;
+ *   bias    [Co] in dtype or NULL; out [M, Co] in dtype
+ *   neighbor_map [M, V] int32 (-1 = missing); masks / order from the map build, or NULL
+ *   (NULL masks = every offset treated as active; NULL order = identity)
+ * Replaces implicit_gemm.py:59-86 and the EXPLICIT_GEMM forward of ops:76-86. */
+int spconv_submanifold_conv_forward(
+    const void *feats, int dtype, int64_t num_coords, int Ci,
+    const void *weight, const void *bias, int Co, int kernel_volume,
+    const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
+    void *out, int32_t *status, void *stream);
+
+/* As spconv_submanifold_conv_forward, with an explicit kernel choice (SPCONV_KERNEL_*).
+ * SPCONV_KERNEL_TCGEN05 returns SPCONV_ERR_UNSUPPORTED for shapes or dtypes it does not
+ * cover. Same reference interface as above. */
+int spconv_submanifold_conv_forward_ex(
+    const void *feats, int dtype, int64_t num_coords, int Ci,
+    const void *weight, const void *bias, int Co, int kernel_volume,
+    const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
+    void *out, int32_t *status, void *stream, int kernel_choice);
+
+/* Stage timing, for profiling and for the benchmark's roofline figures.
+ * spconv_stage_timing(max_calls > 0) creates CUDA events on the current device for
+ * max_calls calls of each stage and starts recording, on the launch stream, the device
+ * time of every stage: the workspace memset, insert_kernel, map_kernel and order_kernel of
+ * the map build, and the conv kernel. spconv_stage_timing(0) stops recording and frees the
+ * events. spconv_stage_times_ms waits for the recorded events and writes, for the first
+ * n stages (SPCONV_STAGE_*), the summed milliseconds and the number of recorded launches;
+ * it returns the number of stages written. No reference counterpart (instrumentation). */
+#define SPCONV_STAGE_MEMSET 0
+#define SPCONV_STAGE_INSERT 1
+#define SPCONV_STAGE_MAP 2
+#define SPCONV_STAGE_ORDER 3
+#define SPCONV_STAGE_CONV 4
+#define SPCONV_NUM_STAGES 5
+
+int spconv_stage_timing(int max_calls);
+int spconv_stage_times_ms(double *total_ms, int64_t *launches, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSECONV_B200_H */

@@ -1,0 +1,121 @@
+// Conv entry points and the CUDA-core (SIMT) submanifold-conv kernel.
+//
+// The SIMT kernel covers what the tcgen05 kernel does not: fp32 features (computed with
+// fp32 FMAs, not TF32, so results stay within 1e-4 of a float64 evaluation) and channel
+// counts outside {16, 32, 64, 128}. One thread computes one output element
+//   out[i, co] = bias[co] + sum_v sum_ci feats[nbr[i,v], ci] * weight[co, v, ci]
+// over the valid neighbours of row i, accumulating in fp32 and rounding once.
+#include "common.cuh"
+#include "conv_internal.h"
+
+namespace spconv {
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+conv_simt_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
+                 const T *__restrict__ bias, const int32_t *__restrict__ nbr,
+                 int64_t M, int Ci, int Co, int V, T *__restrict__ out) {
+    const int64_t total = M * (int64_t)Co;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = idx / Co;
+        const int co = (int)(idx - row * Co);
+        const int32_t *nr = nbr + row * V;
+        float acc = 0.0f;
+        for (int v = 0; v < V; ++v) {
+            const int32_t n = __ldg(nr + v);
+            if (n < 0 || n >= M) continue;       // rows outside the feature table read as missing
+            const T *f = feats + (int64_t)n * Ci;
+            const T *w = weight + ((int64_t)co * V + v) * Ci;
+            for (int ci = 0; ci < Ci; ++ci)
+                acc = fmaf(dtype_traits<T>::to_f(__ldg(f + ci)), dtype_traits<T>::to_f(__ldg(w + ci)), acc);
+        }
+        if (bias) acc += dtype_traits<T>::to_f(__ldg(bias + co));
+        out[idx] = dtype_traits<T>::from_f(acc);
+    }
+}
+
+int launch_conv_simt(const ConvArgs &a) {
+    const int64_t total = a.M * (int64_t)a.Co;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148LL * 64) blocks = 148LL * 64;
+    if (blocks < 1) blocks = 1;
+    switch (a.dtype) {
+        case SPCONV_F32:
+            conv_simt_kernel<float><<<(int)blocks, 256, 0, a.stream>>>(
+                (const float *)a.feats, (const float *)a.weight, (const float *)a.bias, a.nbr,
+                a.M, a.Ci, a.Co, a.V, (float *)a.out);
+            break;
+        case SPCONV_F16:
+            conv_simt_kernel<__half><<<(int)blocks, 256, 0, a.stream>>>(
+                (const __half *)a.feats, (const __half *)a.weight, (const __half *)a.bias, a.nbr,
+                a.M, a.Ci, a.Co, a.V, (__half *)a.out);
+            break;
+        case SPCONV_BF16:
+            conv_simt_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, a.stream>>>(
+                (const __nv_bfloat16 *)a.feats, (const __nv_bfloat16 *)a.weight,
+                (const __nv_bfloat16 *)a.bias, a.nbr, a.M, a.Ci, a.Co, a.V, (__nv_bfloat16 *)a.out);
+            break;
+        default:
+            set_error("unsupported dtype code %d", a.dtype);
+            return SPCONV_ERR_ARG;
+    }
+    return check_launch("conv_simt_kernel");
+}
+
+}  // namespace spconv
+
+using namespace spconv;
+
+static int launch_conv(const ConvArgs &a, int kernel_choice);
+
+extern "C" int spconv_submanifold_conv_forward_ex(
+    const void *feats, int dtype, int64_t M, int Ci,
+    const void *weight, const void *bias, int Co, int V,
+    const int32_t *nbr, const uint32_t *masks, const int32_t *order,
+    void *out, int32_t *status, void *stream, int kernel_choice) {
+    SPCONV_REQUIRE(M >= 0 && M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld out of range", (long long)M);
+    SPCONV_REQUIRE(Ci > 0 && Co > 0, SPCONV_ERR_ARG, "channels must be positive (Ci=%d Co=%d)", Ci, Co);
+    SPCONV_REQUIRE(V > 0 && V <= 1024, SPCONV_ERR_ARG, "kernel volume %d out of range [1, 1024]", V);
+    SPCONV_REQUIRE(dtype == SPCONV_F32 || dtype == SPCONV_F16 || dtype == SPCONV_BF16,
+                   SPCONV_ERR_ARG, "unsupported dtype code %d", dtype);
+    SPCONV_REQUIRE(kernel_choice >= SPCONV_KERNEL_AUTO && kernel_choice <= SPCONV_KERNEL_TCGEN05,
+                   SPCONV_ERR_ARG, "unknown kernel choice %d", kernel_choice);
+    if (M == 0) return SPCONV_OK;
+    SPCONV_REQUIRE(feats && weight && nbr && out, SPCONV_ERR_ARG, "null pointer argument");
+    ConvArgs a{feats, dtype, M, Ci, weight, bias, Co, V, spconv_mask_words(V), nbr, masks, order,
+               out, status, (cudaStream_t)stream};
+    stage_mark(SPCONV_STAGE_CONV, 0, a.stream);
+    const int rc = launch_conv(a, kernel_choice);
+    if (rc == SPCONV_OK) stage_mark(SPCONV_STAGE_CONV, 1, a.stream);
+    return rc;
+}
+
+static int launch_conv(const ConvArgs &a, int kernel_choice) {
+    const int dtype = a.dtype, Ci = a.Ci, Co = a.Co, V = a.V;
+    const void *feats = a.feats, *weight = a.weight, *out = a.out;
+    const bool tc = tc_supported(dtype, Ci, Co, V);
+    if (kernel_choice == SPCONV_KERNEL_TCGEN05) {
+        if (!tc) {
+            set_error("tcgen05 conv does not cover dtype=%d Ci=%d Co=%d", dtype, Ci, Co);
+            return SPCONV_ERR_UNSUPPORTED;
+        }
+        SPCONV_REQUIRE(((uintptr_t)feats & 15u) == 0 && ((uintptr_t)weight & 15u) == 0 &&
+                       ((uintptr_t)out & 15u) == 0, SPCONV_ERR_ARG,
+                       "tcgen05 conv needs 16-byte aligned feats/weight/out");
+        return launch_conv_tc(a);
+    }
+    if (kernel_choice == SPCONV_KERNEL_AUTO && tc && ((uintptr_t)feats & 15u) == 0 &&
+        ((uintptr_t)weight & 15u) == 0 && ((uintptr_t)out & 15u) == 0)
+        return launch_conv_tc(a);
+    return launch_conv_simt(a);
+}
+
+extern "C" int spconv_submanifold_conv_forward(
+    const void *feats, int dtype, int64_t M, int Ci,
+    const void *weight, const void *bias, int Co, int V,
+    const int32_t *nbr, const uint32_t *masks, const int32_t *order,
+    void *out, int32_t *status, void *stream) {
+    return spconv_submanifold_conv_forward_ex(feats, dtype, M, Ci, weight, bias, Co, V, nbr, masks,
+                                              order, out, status, stream, SPCONV_KERNEL_AUTO);
+}

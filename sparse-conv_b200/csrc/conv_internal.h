@@ -1,0 +1,31 @@
+// Internal interface between the conv entry points (conv.cu) and the kernel launchers.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace spconv {
+
+struct ConvArgs {
+    const void *feats;
+    int dtype;
+    int64_t M;
+    int Ci;
+    const void *weight;
+    const void *bias;
+    int Co;
+    int V;
+    int MW;
+    const int32_t *nbr;
+    const uint32_t *masks;
+    const int32_t *order;
+    void *out;
+    int32_t *status;
+    cudaStream_t stream;
+};
+
+bool tc_supported(int dtype, int Ci, int Co, int V);
+int launch_conv_tc(const ConvArgs &a);
+int launch_conv_simt(const ConvArgs &a);
+
+}  // namespace spconv

@@ -1,0 +1,323 @@
+"""ctypes binding of ``libsparseconv_b200.so`` (the C ABI declared in
+``include/sparseconv_b200.h``) plus the tensor-level helpers the front end calls.
+
+There is no CPU fallback: if the library is missing, or a tensor is not on a CUDA device,
+every call raises. Outputs are allocated from torch's caching allocator and every launch
+goes to ``torch.cuda.current_stream()``.
+
+Device-side problems (coordinates out of range, a full table, a kernel wait limit) are
+OR-ed into a per-device int32 status word. After each op the word is copied
+asynchronously to pinned host memory; the next op on that device (or an explicit
+``check_errors()``) raises ``RuntimeError`` if a bit is set. With the environment variable
+``SPARSECONV_SYNC_CHECK=1`` each op synchronises and checks at once.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libsparseconv_b200.so")
+
+SPCONV_OK, SPCONV_ERR_ARG, SPCONV_ERR_CUDA, SPCONV_ERR_UNSUPPORTED = 0, 1, 2, 3
+STATUS_COORD_RANGE, STATUS_TABLE_FULL, STATUS_DUPLICATE, STATUS_WAIT_TIMEOUT = 1, 2, 4, 8
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
+
+_c_i64, _c_int, _c_void_p = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+
+# name -> (restype, argtypes); the order mirrors include/sparseconv_b200.h
+SIGNATURES = {
+    "spconv_abi_version": (_c_int, []),
+    "spconv_last_error": (ctypes.c_char_p, []),
+    "spconv_hashmap_capacity": (_c_i64, [_c_i64]),
+    "spconv_mask_words": (_c_int, [_c_int]),
+    "spconv_neighbor_map_workspace_bytes": (_c_i64, [_c_i64, _c_int, _c_int, _c_int, _c_int]),
+    "spconv_build_submanifold_neighbor_map": (_c_int, [
+        _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int,
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+        _c_void_p, _c_i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_submanifold_conv_forward": (_c_int, [
+        _c_void_p, _c_int, _c_i64, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_submanifold_conv_forward_ex": (_c_int, [
+        _c_void_p, _c_int, _c_i64, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int]),
+    "spconv_stage_timing": (_c_int, [_c_int]),
+    "spconv_stage_times_ms": (_c_int, [_c_void_p, _c_void_p, _c_int]),
+}
+
+STAGES = ("memset", "insert", "map", "order", "conv")
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path: Optional[str] = None) -> ctypes.CDLL:
+    """Load the CUDA library (once). Raises RuntimeError if it has not been built."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise RuntimeError(
+            f"sparseconv CUDA library not found at {p}; build it with "
+            "`python sparse-conv_b200/build.py` (there is no CPU fallback)")
+    lib = ctypes.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.spconv_abi_version() != 1:
+        raise RuntimeError("sparseconv CUDA library ABI version mismatch")
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _raise(rc: int, what: str) -> None:
+    msg = load_library().spconv_last_error().decode(errors="replace")
+    if rc == SPCONV_ERR_ARG:
+        raise ValueError(f"{what}: {msg}")
+    if rc == SPCONV_ERR_UNSUPPORTED:
+        raise NotImplementedError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg}")
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "sparseconv runs on CUDA devices only (no CPU fallback); got a tensor on "
+                f"{t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+# ---------------------------------------------------------------------------------------
+# Device status word and deferred checks.
+# ---------------------------------------------------------------------------------------
+class _DeviceStatus:
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = torch.cuda.Event()
+        self.pending = False
+
+
+_status = {}
+
+
+def status_word(device: torch.device) -> _DeviceStatus:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _status.get(idx)
+    if st is None:
+        with _lock:
+            st = _status.get(idx)
+            if st is None:
+                st = _DeviceStatus(torch.device("cuda", idx))
+                _status[idx] = st
+    return st
+
+
+def describe_status(bits: int) -> str:
+    parts = []
+    if bits & STATUS_COORD_RANGE:
+        parts.append("a coordinate lies outside the spatial shape [0,N)x[0,W)x[0,H)x[0,D)")
+    if bits & STATUS_TABLE_FULL:
+        parts.append("the coordinate hash table overflowed")
+    if bits & STATUS_WAIT_TIMEOUT:
+        parts.append("a kernel-internal wait reached its time limit")
+    return "; ".join(parts)
+
+
+_FATAL_BITS = STATUS_COORD_RANGE | STATUS_TABLE_FULL | STATUS_WAIT_TIMEOUT
+
+
+def _inspect(st: _DeviceStatus) -> None:
+    bits = int(st.host.item())
+    st.pending = False
+    if bits & _FATAL_BITS:
+        st.word.zero_()
+        raise RuntimeError(f"sparseconv device error: {describe_status(bits)} (status bits {bits:#x})")
+
+
+def after_launch(device: torch.device) -> None:
+    """Queue the status read-back of this op; check at once if SPARSECONV_SYNC_CHECK=1."""
+    st = status_word(device)
+    stream = torch.cuda.current_stream(device)
+    st.host.copy_(st.word, non_blocking=True)
+    st.event.record(stream)
+    st.pending = True
+    if os.environ.get("SPARSECONV_SYNC_CHECK", "0") == "1":
+        st.event.synchronize()
+        _inspect(st)
+
+
+def before_launch(device: torch.device) -> None:
+    """Raise for an error found by an earlier op on this device, if its read-back landed."""
+    st = status_word(device)
+    if st.pending and st.event.query():
+        _inspect(st)
+
+
+def check_errors(device: Optional[torch.device] = None) -> int:
+    """Synchronise with the device's status read-back and raise on an error.
+
+    Returns the status bits seen (duplicate coordinates are reported, not raised).
+    """
+    devs = [status_word(device)] if device is not None else list(_status.values())
+    bits = 0
+    for st in devs:
+        if st.pending:
+            st.event.synchronize()
+        torch.cuda.synchronize(st.device)
+        st.host.copy_(st.word)
+        bits |= int(st.host.item())
+        _inspect(st)
+    return bits
+
+
+def reset_status(device: Optional[torch.device] = None) -> None:
+    for st in ([status_word(device)] if device is not None else list(_status.values())):
+        st.word.zero_()
+        st.pending = False
+
+
+# ---------------------------------------------------------------------------------------
+# Tensor-level calls.
+# ---------------------------------------------------------------------------------------
+def mask_words(kernel_volume: int) -> int:
+    return int(load_library().spconv_mask_words(int(kernel_volume)))
+
+
+def hashmap_capacity(num_coords: int) -> int:
+    return int(load_library().spconv_hashmap_capacity(int(num_coords)))
+
+
+def workspace_bytes(num_coords: int, batch: int, W: int, H: int, D: int) -> int:
+    return int(load_library().spconv_neighbor_map_workspace_bytes(int(num_coords), batch, W, H, D))
+
+
+def build_neighbor_map(coords: torch.Tensor, batch: int, W: int, H: int, D: int,
+                       kernel_size: Sequence[int], dilation: Sequence[int],
+                       workspace: Optional[torch.Tensor] = None,
+                       ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Kernel map of ``coords`` ([M,4] int32 on CUDA): (neighbor_map [M,V] int32,
+    masks [M,ceil(V/32)] int32 bit patterns, order [M] int32)."""
+    lib = load_library()
+    dev = _require_cuda(coords)
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] != 4:
+        raise ValueError("coords must be an [M, 4] int32 tensor")
+    if not coords.is_contiguous():
+        raise ValueError("coords must be contiguous")
+    Kw, Kh, Kd = (int(k) for k in kernel_size)
+    Dw, Dh, Dd = (int(d) for d in dilation)
+    M = int(coords.shape[0])
+    V = Kw * Kh * Kd
+    MW = max(1, mask_words(V))
+    nbr = torch.empty((M, V), dtype=torch.int32, device=dev)
+    masks = torch.empty((M, MW), dtype=torch.int32, device=dev)
+    order = torch.empty((M,), dtype=torch.int32, device=dev)
+    if M == 0:
+        return nbr, masks, order
+    need = workspace_bytes(M, batch, W, H, D)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty((need,), dtype=torch.uint8, device=dev)
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_build_submanifold_neighbor_map(
+        coords.data_ptr(), M, int(batch), int(W), int(H), int(D), Kw, Kh, Kd, Dw, Dh, Dd,
+        workspace.data_ptr(), need, nbr.data_ptr(), masks.data_ptr(), order.data_ptr(),
+        st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_build_submanifold_neighbor_map")
+    return nbr, masks, order
+
+
+def conv_forward(feats: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+                 nbr: torch.Tensor, masks: Optional[torch.Tensor], order: Optional[torch.Tensor],
+                 kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[i] = bias + sum_v feats[nbr[i,v]] @ weight[:, v, :]^T over valid neighbours.
+
+    ``weight`` is [Co, V, Ci] (or [Co, Kw, Kh, Kd, Ci]) in the dtype of ``feats``.
+    """
+    lib = load_library()
+    dev = _require_cuda(feats, weight, bias, nbr, masks, order)
+    if feats.dtype not in DTYPE_CODES:
+        raise TypeError(f"unsupported feature dtype {feats.dtype}")
+    if not feats.is_contiguous():
+        raise ValueError("feats must be contiguous")
+    M, Ci = int(feats.shape[0]), int(feats.shape[1])
+    Co = int(weight.shape[0])
+    V = int(nbr.shape[1]) if nbr.dim() == 2 else 0
+    if nbr.shape[0] != M:
+        raise ValueError(f"neighbor map has {nbr.shape[0]} rows for {M} feature rows")
+    w = weight.reshape(Co, V, Ci)
+    if w.dtype != feats.dtype:
+        w = w.to(feats.dtype)
+    w = w.contiguous()
+    b = None
+    if bias is not None:
+        b = bias.to(feats.dtype).contiguous()
+        if b.numel() != Co:
+            raise ValueError(f"bias has {b.numel()} entries for {Co} output channels")
+    nb = nbr.view(torch.int32) if nbr.dtype == torch.uint32 else nbr
+    if nb.dtype != torch.int32 or not nb.is_contiguous():
+        raise ValueError("neighbor map must be a contiguous [M, V] int32/uint32 tensor")
+    mk = None
+    if masks is not None:
+        mk = masks.view(torch.int32) if masks.dtype == torch.uint32 else masks
+        if mk.dtype != torch.int32 or mk.shape[0] != M or not mk.is_contiguous():
+            raise ValueError("masks must be a contiguous [M, ceil(V/32)] 32-bit tensor")
+    od = None
+    if order is not None:
+        if order.dtype != torch.int32 or order.numel() != M or not order.is_contiguous():
+            raise ValueError("order must be a contiguous [M] int32 tensor")
+        od = order
+    if out is None:
+        out = torch.empty((M, Co), dtype=feats.dtype, device=dev)
+    if M == 0:
+        return out
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_submanifold_conv_forward_ex(
+        feats.data_ptr(), DTYPE_CODES[feats.dtype], M, Ci, w.data_ptr(),
+        None if b is None else b.data_ptr(), Co, V, nb.data_ptr(),
+        None if mk is None else mk.data_ptr(), None if od is None else od.data_ptr(),
+        out.data_ptr(), st.word.data_ptr(), _stream_ptr(dev), int(kernel))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_submanifold_conv_forward")
+    return out
+
+
+def stage_timing(max_calls: int) -> None:
+    """Start (max_calls > 0) or stop (0) per-stage device timing inside the library."""
+    rc = load_library().spconv_stage_timing(int(max_calls))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_stage_timing")
+
+
+def stage_times_ms() -> dict:
+    """{stage: (summed ms, launches)} for the calls recorded since stage_timing(n)."""
+    import numpy as np
+    ms = np.zeros(len(STAGES), dtype=np.float64)
+    cnt = np.zeros(len(STAGES), dtype=np.int64)
+    n = load_library().spconv_stage_times_ms(ms.ctypes.data, cnt.ctypes.data, len(STAGES))
+    if n < 0:
+        _raise(SPCONV_ERR_CUDA, "spconv_stage_times_ms")
+    return {STAGES[i]: (float(ms[i]), int(cnt[i])) for i in range(n)}

@@ -1,0 +1,93 @@
+"""The C-ABI library loads on a machine without a GPU, exports every symbol that
+include/sparseconv_b200.h declares, and its host-side sizing and argument validation
+behave as documented (none of these calls reach the device)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from sparseconv import _native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER_DIR = os.path.join(ROOT, "include")
+
+
+def _declared_functions():
+    names = []
+    for fn in sorted(os.listdir(HEADER_DIR)):
+        if fn.endswith(".h"):
+            text = open(os.path.join(HEADER_DIR, fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names += re.findall(r"\b(spconv_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _native.load_library()
+
+
+def test_header_declares_entry_points():
+    names = _declared_functions()
+    assert "spconv_build_submanifold_neighbor_map" in names
+    assert "spconv_submanifold_conv_forward" in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in _declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        assert name in _native.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_abi_version(lib):
+    assert lib.spconv_abi_version() == 1
+
+
+def test_hashmap_capacity(lib):
+    assert lib.spconv_hashmap_capacity(0) == 1024
+    assert lib.spconv_hashmap_capacity(512) == 1024
+    assert lib.spconv_hashmap_capacity(513) == 2048
+    for m in (1000, 168546, 2_000_000, 1_342_011):
+        cap = lib.spconv_hashmap_capacity(m)
+        assert cap >= 2 * m and cap & (cap - 1) == 0 and cap < 4 * m + 1024
+
+
+def test_mask_words(lib):
+    assert [lib.spconv_mask_words(v) for v in (1, 27, 32, 33, 125, 343)] == [1, 1, 1, 2, 4, 11]
+
+
+def test_workspace_bytes(lib):
+    small = lib.spconv_neighbor_map_workspace_bytes(1000, 4, 128, 128, 128)
+    big_vol = lib.spconv_neighbor_map_workspace_bytes(1000, 2, 2048, 2048, 1024)
+    assert small >= 8 * 2048 and big_vol > small          # 64-bit keys add a value array
+    assert lib.spconv_neighbor_map_workspace_bytes(-1, 1, 1, 1, 1) == -1
+
+
+def test_argument_validation_before_any_launch(lib):
+    nb = lib.spconv_build_submanifold_neighbor_map
+    # bad kernel size / dilation / shape / count: SPCONV_ERR_ARG with a message
+    assert nb(None, 10, 1, 4, 4, 4, 0, 3, 3, 1, 1, 1, None, 0, None, None, None, None, None) == 1
+    assert b"kernel size" in lib.spconv_last_error()
+    assert nb(None, 10, 1, 4, 4, 4, 3, 3, 3, 0, 1, 1, None, 0, None, None, None, None, None) == 1
+    assert nb(None, -1, 1, 4, 4, 4, 3, 3, 3, 1, 1, 1, None, 0, None, None, None, None, None) == 1
+    assert nb(None, 10, 0, 4, 4, 4, 3, 3, 3, 1, 1, 1, None, 0, None, None, None, None, None) == 1
+    assert nb(None, 10, 1, 4, 4, 4, 11, 11, 11, 1, 1, 1, None, 0, None, None, None, None, None) == 1
+    # null buffers for a non-empty input
+    assert nb(None, 10, 1, 4, 4, 4, 3, 3, 3, 1, 1, 1, None, 0, None, None, None, None, None) == 1
+    # empty input: nothing to do
+    assert nb(None, 0, 1, 4, 4, 4, 3, 3, 3, 1, 1, 1, None, 0, None, None, None, None, None) == 0
+    cf = lib.spconv_submanifold_conv_forward
+    assert cf(None, 7, 10, 3, None, None, 3, 27, None, None, None, None, None, None) == 1   # dtype
+    assert cf(None, 0, 10, 0, None, None, 3, 27, None, None, None, None, None, None) == 1   # Ci
+    assert cf(None, 0, 10, 3, None, None, 3, 2000, None, None, None, None, None, None) == 1  # V
+    assert cf(None, 0, 0, 3, None, None, 3, 27, None, None, None, None, None, None) == 0    # M=0
+    ex = lib.spconv_submanifold_conv_forward_ex
+    assert ex(None, 0, 10, 3, None, None, 3, 27, None, None, None, None, None, None, 9) == 1
+    assert ex(ctypes.c_void_p(16), 0, 10, 3, ctypes.c_void_p(16), None, 3, 27, ctypes.c_void_p(16),
+              None, None, ctypes.c_void_p(16), None, None, 2) == 3        # tcgen05: no fp32 path
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _native.load_library(str(tmp_path / "absent.so"))

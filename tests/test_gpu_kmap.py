@@ -1,0 +1,112 @@
+"""Kernel-map parity on the GPU: the library's map must equal the oracle's (and so the
+reference's) bit for bit; masks and order must be consistent with it. Calls go through
+the C ABI (``sparseconv._native``)."""
+import numpy as np
+import pytest
+import torch
+
+import gpu_cases
+from oracle import oracle
+from sparseconv import _native
+
+pytestmark = pytest.mark.gpu
+
+
+def gpu_map(coords, shape, ks, dil):
+    N, _C, W, H, D = shape
+    c = torch.from_numpy(np.ascontiguousarray(coords)).cuda()
+    nbr, masks, order = _native.build_neighbor_map(c, N, W, H, D, ks, dil)
+    torch.cuda.synchronize()
+    return (nbr.cpu().numpy().view(np.uint32), masks.cpu().numpy().view(np.uint32),
+            order.cpu().numpy())
+
+
+def check_masks_and_order(nbr, masks, order):
+    M, V = nbr.shape
+    MW = (V + 31) // 32
+    assert masks.shape == (M, MW)
+    valid = nbr != 0xFFFFFFFF
+    expect = np.zeros((M, MW), dtype=np.uint64)
+    for v in range(V):
+        expect[:, v // 32] |= valid[:, v].astype(np.uint64) << np.uint64(v % 32)
+    np.testing.assert_array_equal(masks.astype(np.uint64), expect)
+    assert np.array_equal(np.sort(order), np.arange(M, dtype=np.int32)), "order is a permutation"
+    if M:
+        cls = np.minimum(valid.sum(1) - 1, 15)[order]
+        assert np.all(np.diff(cls) >= 0), "order groups voxels by neighbour-count class"
+
+
+@pytest.mark.parametrize("name", sorted(gpu_cases.small_cases()))
+def test_small_cases_bit_exact(name):
+    coords, shape, ks, dil = gpu_cases.small_cases()[name]
+    nbr, masks, order = gpu_map(coords, shape, ks, dil)
+    np.testing.assert_array_equal(nbr, oracle.neighbor_map(coords, shape, ks, dil))
+    check_masks_and_order(nbr, masks, order)
+
+
+@pytest.mark.parametrize("name", ["cube", "lidar", "indoor", "wide3", "wide5"])
+def test_full_size_configs_bit_exact(name):
+    w = gpu_cases.workload(name)
+    nbr, masks, order = gpu_map(w.coords, w.shape, w.kernel_size, w.dilation)
+    ref = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation)
+    np.testing.assert_array_equal(nbr, ref)
+    check_masks_and_order(nbr, masks, order)
+
+
+def test_readme_toy_known_answer():
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "readme_toy.npz"))
+    nbr, masks, order = gpu_map(g["coords"], tuple(g["shape"]), (3, 3, 3), (1, 1, 1))
+    np.testing.assert_array_equal(nbr, g["neighbor_map"])
+
+
+def test_empty_input():
+    nbr, masks, order = gpu_map(np.zeros((0, 4), np.int32), (1, 1, 4, 4, 4), (3, 3, 3), (1, 1, 1))
+    assert nbr.shape == (0, 27) and order.shape == (0,)
+
+
+def test_unsorted_input_matches_oracle():
+    coords, shape, ks, dil = gpu_cases.small_cases()["rand3"]
+    perm = np.random.default_rng(0).permutation(coords.shape[0])
+    c = np.ascontiguousarray(coords[perm])
+    nbr, masks, order = gpu_map(c, shape, ks, dil)
+    np.testing.assert_array_equal(nbr, oracle.neighbor_map(c, shape, ks, dil))
+
+
+def test_duplicate_coordinates_keep_highest_row():
+    coords = np.array([[0, 1, 1, 1], [0, 1, 1, 2], [0, 1, 1, 1], [0, 3, 3, 3]], dtype=np.int32)
+    _native.reset_status()
+    nbr, _, _ = gpu_map(coords, (1, 1, 5, 5, 5), (3, 3, 3), (1, 1, 1))
+    np.testing.assert_array_equal(nbr, oracle.neighbor_map(coords, (1, 1, 5, 5, 5), (3, 3, 3)))
+    bits = _native.check_errors(torch.device("cuda", 0))
+    assert bits & _native.STATUS_DUPLICATE
+    _native.reset_status()
+
+
+def test_out_of_range_coordinates_raise():
+    coords = torch.tensor([[0, 1, 1, 1], [0, 5, 1, 1]], dtype=torch.int32, device="cuda")
+    _native.reset_status()
+    _native.build_neighbor_map(coords, 1, 5, 5, 5, (3, 3, 3), (1, 1, 1))
+    with pytest.raises(RuntimeError, match="outside the spatial shape"):
+        _native.check_errors(torch.device("cuda", 0))
+    _native.reset_status()
+
+
+def test_repeated_builds_reuse_workspace():
+    coords, shape, ks, dil = gpu_cases.small_cases()["rand5"]
+    a = gpu_map(coords, shape, ks, dil)[0]
+    b = gpu_map(coords, shape, ks, dil)[0]
+    np.testing.assert_array_equal(a, b)
+
+
+def test_non_default_stream():
+    coords, shape, ks, dil = gpu_cases.small_cases()["dense3"]
+    N, _C, W, H, D = shape
+    s = torch.cuda.Stream()
+    c = torch.from_numpy(coords).cuda()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        nbr, masks, order = _native.build_neighbor_map(c, N, W, H, D, ks, dil)
+    s.synchronize()
+    np.testing.assert_array_equal(nbr.cpu().numpy().view(np.uint32),
+                                  oracle.neighbor_map(coords, shape, ks, dil))
