@@ -97,6 +97,39 @@ int spconv_build_submanifold_neighbor_map(
     int32_t *neighbor_map, uint32_t *masks, int32_t *order,
     int32_t *status, void *stream);
 
+/* Largest num_coords that spconv_build_submanifold_neighbor_map_noalloc accepts. */
+#define SPCONV_NOALLOC_MAX_COORDS 524288
+
+/* Kernel-map build that allocates nothing: the same result as
+ * spconv_build_submanifold_neighbor_map, but the hash table and order histogram live in a
+ * fixed scratch array compiled into this library (a file-scope __device__ array of about
+ * 12 MiB, resident on every GPU that loads the library until the process exits), so the
+ * caller passes only coords and the outputs.
+ *
+ * For callers that cannot allocate device memory where the map is built: plugin hosts that
+ * hand an operator only its input and output buffers and no allocator, loops whose memory is
+ * fixed at start-up and must not call cudaMalloc (it can synchronise the device and can fail
+ * under memory pressure), and runtimes whose allocator is not safe to call at that point.
+ *
+ * Limits and rules:
+ *   - num_coords <= SPCONV_NOALLOC_MAX_COORDS; larger inputs return SPCONV_ERR_ARG (use the
+ *     workspace entry point for them);
+ *   - the first call on a device looks up the scratch array's device address for that device
+ *     (cudaGetSymbolAddress, with the stream's device current); make that first call before
+ *     any stream capture begins;
+ *   - every call on a device shares the one scratch array and leaves it holding that call's
+ *     table; each call clears what it uses first. Calls whose execution overlaps on the GPU
+ *     (different streams without ordering, or several host threads) race on the array and
+ *     give wrong maps: order them on one stream or synchronise between them.
+ * No counterpart in the reference (its table is always allocated by the caller,
+ * ops/utils.py:3-16). */
+int spconv_build_submanifold_neighbor_map_noalloc(
+    const int32_t *coords, int64_t num_coords,
+    int batch, int W, int H, int D,
+    int Kw, int Kh, int Kd, int Dw, int Dh, int Dd,
+    int32_t *neighbor_map, uint32_t *masks, int32_t *order,
+    int32_t *status, void *stream);
+
 /* Submanifold conv forward over a kernel map:
  *   out[i, co] = bias[co] + sum_v sum_ci feats[nbr[i,v], ci] * weight[co, v, ci]
  * with fp32 accumulation, rounded once to `dtype` (no atomics, each output row written once).

@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdarg>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -400,4 +401,75 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     if (int rc = check_launch("order_kernel")) return rc;
     stage_mark(SPCONV_STAGE_ORDER, 1, stream);
     return SPCONV_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant: the workspace is a fixed file-scope device array.
+//
+// Callers that cannot allocate device memory at the point of the call (operator plugin
+// hosts that pass only input/output buffers, fixed-memory real-time loops, runtimes whose
+// allocator must not run there) get the same map from here without a workspace argument.
+// The array is sized for SPCONV_NOALLOC_MAX_COORDS voxels with 64-bit keys (the larger
+// layout), about 12 MiB; every GPU that loads the library holds it until the process exits.
+// In host code `g_noalloc_scratch` names a host-side stand-in, not device memory: its device
+// address is looked up per device with cudaGetSymbolAddress and only that address is passed on.
+// ---------------------------------------------------------------------------------------
+namespace spconv {
+
+constexpr int64_t noalloc_capacity() {
+    int64_t cap = 1024;
+    while (cap < 2 * (int64_t)SPCONV_NOALLOC_MAX_COORDS) cap <<= 1;
+    return cap;
+}
+constexpr int64_t align256c(int64_t x) { return (x + 255) & ~int64_t(255); }
+constexpr int64_t kNoAllocScratchBytes =
+    align256c(noalloc_capacity() * 8) + align256c(noalloc_capacity() * 4) +
+    2 * align256c(kOrderBuckets * 4) + 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device; looked up once per device.
+static int noalloc_scratch(void **out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+    SPCONV_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, SPCONV_ERR_ARG,
+                   "device ordinal %d exceeds the %d devices the scratch table tracks", dev, kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_dev_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            set_error("cudaGetSymbolAddress of the no-alloc scratch failed on device %d: %s",
+                      dev, cudaGetErrorString(e));
+            return SPCONV_ERR_CUDA;
+        }
+        g_noalloc_dev_ptr[dev] = p;
+    }
+    *out = g_noalloc_dev_ptr[dev];
+    return SPCONV_OK;
+}
+
+}  // namespace spconv
+
+extern "C" int spconv_build_submanifold_neighbor_map_noalloc(
+    const int32_t *coords, int64_t M,
+    int batch, int W, int H, int D,
+    int Kw, int Kh, int Kd, int Dw, int Dh, int Dd,
+    int32_t *neighbor_map, uint32_t *masks, int32_t *order,
+    int32_t *status, void *stream) {
+    SPCONV_REQUIRE(M <= (int64_t)SPCONV_NOALLOC_MAX_COORDS, SPCONV_ERR_ARG,
+                   "num_coords %lld exceeds the no-alloc limit of %d coordinates "
+                   "(use spconv_build_submanifold_neighbor_map with a workspace)",
+                   (long long)M, (int)SPCONV_NOALLOC_MAX_COORDS);
+    void *scratch = nullptr;
+    if (M > 0) {
+        if (int rc = noalloc_scratch(&scratch)) return rc;
+    }
+    return spconv_build_submanifold_neighbor_map(
+        coords, M, batch, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, scratch, kNoAllocScratchBytes,
+        neighbor_map, masks, order, status, stream);
 }

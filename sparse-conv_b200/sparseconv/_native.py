@@ -26,6 +26,7 @@ SPCONV_OK, SPCONV_ERR_ARG, SPCONV_ERR_CUDA, SPCONV_ERR_UNSUPPORTED = 0, 1, 2, 3
 STATUS_COORD_RANGE, STATUS_TABLE_FULL, STATUS_DUPLICATE, STATUS_WAIT_TIMEOUT = 1, 2, 4, 8
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
+NOALLOC_MAX_COORDS = 524288   # SPCONV_NOALLOC_MAX_COORDS
 
 _c_i64, _c_int, _c_void_p = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
 
@@ -46,6 +47,10 @@ SIGNATURES = {
     "spconv_submanifold_conv_forward_ex": (_c_int, [
         _c_void_p, _c_int, _c_i64, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int]),
+    "spconv_build_submanifold_neighbor_map_noalloc": (_c_int, [
+        _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int,
+        _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_stage_timing": (_c_int, [_c_int]),
     "spconv_stage_times_ms": (_c_int, [_c_void_p, _c_void_p, _c_int]),
 }
