@@ -98,7 +98,7 @@ int spconv_build_submanifold_neighbor_map(
     int32_t *status, void *stream);
 
 /* Largest num_coords that spconv_build_submanifold_neighbor_map_noalloc accepts. */
-#define SPCONV_NOALLOC_MAX_COORDS 524288
+#define SPCONV_NOALLOC_MAX_COORDS 262144
 
 /* Kernel-map build that allocates nothing: the same result as
  * spconv_build_submanifold_neighbor_map, but the hash table and order histogram live in a

@@ -116,6 +116,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t addr, uint32_t parity
     }
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t addr) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n"
+                 :: "r"(addr) : "memory");
+}
+// Arrive on the mbarrier once every cp.async issued so far by this thread has landed; the
+// arrival counts toward the barrier's expected count (.noinc).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t addr) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" :: "r"(addr) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+// Named barrier among `count` threads (id 1..15; id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;\n" :: "r"(id), "r"(count) : "memory");
+}
+// Bounded wait that also gives up when another role of the CTA has flagged an abort.
+// On timeout it sets the flag itself. Returns false when the caller must abandon its work.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint32_t addr, uint32_t parity,
+                                                   volatile int *abort_flag) {
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait(addr, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------
 // tcgen05 (sm_100a): TMEM allocation, MMA issue/commit, TMEM -> register loads.
 // ---------------------------------------------------------------------------------------

@@ -35,6 +35,29 @@ conv_simt_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
     }
 }
 
+int occupancy_per_sm(const void *kern, int threads, int smem_dynamic) {
+    cudaFuncAttributes fa{};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+    }
+    int smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0, blk_sm = 0;
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&thr_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+    cudaDeviceGetAttribute(&blk_sm, cudaDevAttrMaxBlocksPerMultiprocessor, dev);
+    const int warps = (threads + 31) / 32;
+    const int regs_warp = ((fa.numRegs * 32 + 255) / 256) * 256;      // 256-register granularity
+    int occ = blk_sm > 0 ? blk_sm : 32;
+    const int per_cta_smem = smem_dynamic + (int)fa.sharedSizeBytes + reserved;
+    if (per_cta_smem > 0 && smem_sm / per_cta_smem < occ) occ = smem_sm / per_cta_smem;
+    if (regs_warp > 0 && regs_sm / (regs_warp * warps) < occ) occ = regs_sm / (regs_warp * warps);
+    if (thr_sm / threads < occ) occ = thr_sm / threads;
+    return occ < 1 ? 1 : occ;
+}
+
 int launch_conv_simt(const ConvArgs &a) {
     const int64_t total = a.M * (int64_t)a.Co;
     int64_t blocks = (total + 255) / 256;

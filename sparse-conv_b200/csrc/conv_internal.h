@@ -25,6 +25,11 @@ struct ConvArgs {
 };
 
 bool tc_supported(int dtype, int Ci, int Co, int V);
+
+// Resident CTAs per SM for `kern` at `threads` threads and `smem_dynamic` bytes of dynamic
+// shared memory, from the kernel's attributes and the device limits (shared memory incl. the
+// per-CTA reservation, registers at warp granularity, threads, CTAs).
+int occupancy_per_sm(const void *kern, int threads, int smem_dynamic);
 int launch_conv_tc(const ConvArgs &a);
 int launch_conv_simt(const ConvArgs &a);
 

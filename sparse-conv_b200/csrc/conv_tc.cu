@@ -23,7 +23,7 @@ namespace spconv {
 
 constexpr int kTcThreads = 128;
 constexpr int kTileM = 128;
-constexpr int kTcStages = 2;
+constexpr int kTcStages = 3;
 
 template <int CI, int CO>
 struct TcCfg {
@@ -101,18 +101,23 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
         }
         __syncthreads();
 
+        // Active offsets are consumed in ascending v. The gather of offset j+1 is issued
+        // before waiting for offset j's data, so two gathers are in flight per thread while
+        // the tensor core works on the previous offset.
         const int32_t *nrow = nbr + (int64_t)(row < 0 ? 0 : row) * V;
-        int j = 0, w = 0;
-        uint32_t m = s_maskw[0];
-        for (;;) {
-            while (m == 0u && ++w < MW) m = s_maskw[w];
-            if (m == 0u) break;
-            const int v = w * 32 + __ffs(m) - 1;
-            m &= m - 1u;
-            const int s = (int)(it % kTcStages);
-            const uint32_t use = it / kTcStages;
+        int nact = 0;
+        for (int w = 0; w < MW; ++w) nact += __popc(s_maskw[w]);
+        int iw = 0;                                 // issue-side cursor over the mask words
+        uint32_t im = s_maskw[0];
+        const uint32_t it0 = it;
+        auto issue = [&](int jj) {
+            while (im == 0u && ++iw < MW) im = s_maskw[iw];
+            const int v = iw * 32 + __ffs(im) - 1;
+            im &= im - 1u;
+            const uint32_t slot = it0 + (uint32_t)jj;
+            const int s = (int)(slot % kTcStages);
+            const uint32_t use = slot / kTcStages;
             if (use > 0 && !mbar_wait_bounded(smem_u32(&mbar[s]), (use - 1u) & 1u)) ok = false;
-
             int32_t n = row >= 0 ? __ldg(nrow + v) : -1;
             if (n >= M) n = -1;                   // rows outside the feature table read as missing
             const T *src = feats + (int64_t)(n < 0 ? 0 : n) * CI;
@@ -128,11 +133,23 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
                             weight + ((int64_t)co * V + v) * CI + c * 8, 16u);
             }
             cp_async_commit();
-            cp_async_wait<0>();
+        };
+        if (nact > 0) issue(0);
+        int j = 0;
+        for (; j < nact; ++j) {
+            if (j + 1 < nact) {
+                issue(j + 1);
+                cp_async_wait<1>();               // offset j's group has landed
+            } else {
+                cp_async_wait<0>();
+            }
             fence_proxy_async_smem();
             if (!__syncthreads_and(ok)) { ok = false; break; }
+            const int s = (int)((it0 + (uint32_t)j) % kTcStages);
             if (tid == 0) {
                 tc_fence_after();
+                const uint32_t a_st = a_stage0 + s * Cfg::kABytes;
+                const uint32_t b_st = b_stage0 + s * Cfg::kBBytes;
 #pragma unroll
                 for (int k = 0; k < CI / 16; ++k) {
                     const uint64_t ad = smem_desc_kmajor_noswizzle(a_st + k * 2 * (kTileM * 16), kTileM * 16, 128);
@@ -141,10 +158,12 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
                 }
                 tc_commit(smem_u32(&mbar[s]));
             }
-            ++it;
-            ++j;
         }
-        if (!ok) break;
+        it = it0 + (uint32_t)j;
+        if (!ok) {
+            cp_async_wait<0>();
+            break;
+        }
         if (j > 0) {
             const uint32_t last = it - 1u;
             if (!mbar_wait_bounded(smem_u32(&mbar[last % kTcStages]), (last / kTcStages) & 1u)) ok = false;
@@ -209,18 +228,26 @@ static int launch_tc(const ConvArgs &a) {
     constexpr int kSmemForTmem = (228 * 1024) / (Cfg::kMaxCtasByTmem + 1);
     constexpr int smem = Cfg::kSmemBytes > kSmemForTmem ? Cfg::kSmemBytes : kSmemForTmem;
     static bool attr_done[64] = {false};
+    static int occ_cache[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_done[dev]) {
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr_done[dev]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-            return check_launch("conv_tc set smem attribute");
+            return check_launch("conv_tc: set max dynamic shared memory");
+        // Without a carveout preference the occupancy query (and the launch) may assume a
+        // small shared-memory carveout and allow a single CTA per SM.
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+            return check_launch("conv_tc: set shared memory carveout");
+        int occ = occupancy_per_sm((const void *)kern, kTcThreads, smem);
+        if (occ > Cfg::kMaxCtasByTmem) occ = Cfg::kMaxCtasByTmem;
+        occ_cache[dev] = occ;
         attr_done[dev] = true;
     }
-    int sms = 0, occ = 0;
+    int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTcThreads, smem);
-    if (occ < 1) occ = 1;
-    if (occ > Cfg::kMaxCtasByTmem) occ = Cfg::kMaxCtasByTmem;
+    const int occ = occ_cache[dev];
     const int num_tiles = (int)((a.M + kTileM - 1) / kTileM);
     int grid = sms * occ;
     if (grid > num_tiles) grid = num_tiles;

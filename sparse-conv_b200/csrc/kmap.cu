@@ -31,13 +31,27 @@
 namespace spconv {
 
 constexpr int kOrderBuckets = 4096;    // 16 popcount classes x 256 mask-hash buckets
-constexpr int kMapThreads = 256;
-constexpr int kMapVoxels = 512;        // voxels per map_kernel block
+constexpr int kMapThreads = 128;      // one thread per voxel
 constexpr int kOrderThreads = 256;
-constexpr int kOrderPerThread = 8;     // voxels per thread in order_kernel
+constexpr int kOrderPerThread = 2;     // voxels per thread in order_kernel
 constexpr int kMaxKernelVolume = 1024;
 
 static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// Table capacity for M voxels: the next power of two >= 4M (load <= 0.25) while the table
+// stays within 64 MB (L2-resident next to the streams it serves), else >= 2M (load <= 0.5).
+// Slots are probed in aligned groups of kGroup = 4 (one 32-byte sector per probe).
+constexpr int kGroup = 4;
+constexpr int64_t kLowLoadTableBytes = 64ll << 20;
+constexpr int64_t capacity_for(int64_t M) {
+    int64_t cap = 1024;
+    while (cap < 4 * M) cap <<= 1;
+    if (cap * 8 > kLowLoadTableBytes) {
+        cap = 1024;
+        while (cap < 2 * M) cap <<= 1;
+    }
+    return cap;
+}
 
 struct WsLayout {
     int64_t cap = 0;
@@ -52,7 +66,7 @@ static bool volume_fits_32(int batch, int W, int H, int D) {
 
 static WsLayout ws_layout(int64_t M, bool key64) {
     WsLayout L;
-    L.cap = spconv_hashmap_capacity(M);
+    L.cap = capacity_for(M);
     L.key64 = key64;
     int64_t off = 0;
     L.table = off; off += align256(L.cap * 8);
@@ -79,70 +93,86 @@ __device__ __forceinline__ uint32_t aggregated_inc(uint32_t *counter, uint32_t k
 
 // ---------------------------------------------------------------------------------------
 // Table: packed 64-bit slots for volumes < 2^32 (key = flat index), or 64-bit keys plus a
-// separate value array otherwise. Stored complemented; 0 = empty.
+// separate row array otherwise; stored complemented, so 0 = empty. A key hashes to a group
+// of kGroup consecutive slots (32 bytes); inserts take the first empty slot of the first
+// group with room (linear probing over groups), so a lookup that finds an empty slot in a
+// group without a match can stop: one 32-byte probe settles almost every lookup.
 // ---------------------------------------------------------------------------------------
+// Home group of a 32-bit key: Fibonacci hashing, the top log2(groups) bits of
+// key * 2654435761 (shift = 32 - log2(groups)); consecutive grid keys land far apart.
+__device__ __forceinline__ uint32_t home32(uint32_t key, uint32_t shift) {
+    return (key * 0x9E3779B1u) >> shift;
+}
+
+template <bool KEY64>
+__device__ __forceinline__ uint64_t home_group(uint64_t flat, uint64_t gmask, uint32_t shift) {
+    return KEY64 ? (fmix64(flat) & gmask) : (uint64_t)home32((uint32_t)flat, shift);
+}
+
 template <bool KEY64>
 __device__ __forceinline__ bool table_insert(unsigned long long *table, uint32_t *vals,
-                                             uint64_t mask, uint64_t flat, uint32_t row,
-                                             int32_t *status) {
-    if (!KEY64) {
-        const uint32_t key = (uint32_t)flat;
-        const unsigned long long desired = ~((((unsigned long long)key) << 32) | row);
-        uint64_t s = fmix32(key) & mask;
-        for (uint64_t p = 0; p <= mask; ++p) {
-            const unsigned long long prev = atomicCAS(table + s, 0ull, desired);
-            if (prev == 0ull) return true;
-            if ((uint32_t)((~prev) >> 32) == key) {
-                // Duplicate coordinate: keep the highest row (min of the complement).
-                atomicMin(table + s, desired);
+                                             uint64_t gmask, uint32_t shift, uint64_t flat,
+                                             uint32_t row, int32_t *status) {
+    const unsigned long long desired =
+        KEY64 ? ~(unsigned long long)flat : ~((((unsigned long long)(uint32_t)flat) << 32) | row);
+    uint64_t g = home_group<KEY64>(flat, gmask, shift);
+    for (uint64_t pg = 0; pg <= gmask; ++pg) {
+        unsigned long long *grp = table + g * kGroup;
+#pragma unroll
+        for (int i = 0; i < kGroup; ++i) {
+            unsigned long long cur = grp[i];
+            if (cur == 0ull) {
+                cur = atomicCAS(grp + i, 0ull, desired);
+                if (cur == 0ull) {
+                    if (KEY64) atomicMax(vals + g * kGroup + i, row);
+                    return true;
+                }
+            }
+            const bool same = KEY64 ? (cur == desired) : ((uint32_t)(cur >> 32) == (uint32_t)(desired >> 32));
+            if (same) {
+                // Duplicate coordinate: keep the highest row.
+                if (KEY64) atomicMax(vals + g * kGroup + i, row);
+                else atomicMin(grp + i, desired);        // min of the complement = max row
                 raise_status(status, SPCONV_STATUS_DUPLICATE);
                 return true;
             }
-            s = (s + 1) & mask;
         }
-        return false;
-    } else {
-        const unsigned long long kst = ~(unsigned long long)flat;
-        uint64_t s = fmix64(flat) & mask;
-        for (uint64_t p = 0; p <= mask; ++p) {
-            const unsigned long long prev = atomicCAS(table + s, 0ull, kst);
-            if (prev == 0ull || prev == kst) {
-                if (prev == kst) raise_status(status, SPCONV_STATUS_DUPLICATE);
-                atomicMax(vals + s, row);
-                return true;
-            }
-            s = (s + 1) & mask;
-        }
-        return false;
+        g = (g + 1) & gmask;
     }
+    return false;
 }
 
-// Returns the row of `flat`, -1 if absent, -2 if the probe wrapped the whole table.
+__device__ __forceinline__ void load_group(const unsigned long long *__restrict__ table, uint64_t g,
+                                           unsigned long long (&w)[kGroup]) {
+    const ulonglong2 *p = reinterpret_cast<const ulonglong2 *>(table + g * kGroup);
+    const ulonglong2 a = __ldg(p), b = __ldg(p + 1);
+    w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
+}
+
+// Row of `flat` given its home group's loaded words; continues to later groups while they
+// are full. Returns the row, -1 if absent, -2 if every group was full (table overflow).
 template <bool KEY64>
-__device__ __forceinline__ int32_t table_lookup(const unsigned long long *__restrict__ table,
-                                                const uint32_t *__restrict__ vals,
-                                                uint64_t mask, uint64_t flat) {
-    if (!KEY64) {
-        const uint32_t key = (uint32_t)flat;
-        uint64_t s = fmix32(key) & mask;
-        for (uint64_t p = 0; p <= mask; ++p) {
-            const unsigned long long w = __ldg(table + s);
-            if (w == 0ull) return -1;
-            if ((uint32_t)((~w) >> 32) == key) return (int32_t)(uint32_t)(~w);
-            s = (s + 1) & mask;
+__device__ __forceinline__ int32_t table_resolve(const unsigned long long *__restrict__ table,
+                                                 const uint32_t *__restrict__ vals, uint64_t gmask,
+                                                 uint64_t flat, uint64_t g, unsigned long long (&w)[kGroup]) {
+    const uint32_t nk = ~(uint32_t)flat;
+    const unsigned long long nk64 = ~(unsigned long long)flat;
+    for (uint64_t pg = 0; pg <= gmask; ++pg) {
+        bool empty = false;
+#pragma unroll
+        for (int i = 0; i < kGroup; ++i) {
+            if (KEY64) {
+                if (w[i] == nk64) return (int32_t)__ldg(vals + g * kGroup + i);
+            } else {
+                if ((uint32_t)(w[i] >> 32) == nk && w[i] != 0ull) return (int32_t)(~(uint32_t)w[i]);
+            }
+            empty |= (w[i] == 0ull);
         }
-        return -2;
-    } else {
-        const unsigned long long kst = ~(unsigned long long)flat;
-        uint64_t s = fmix64(flat) & mask;
-        for (uint64_t p = 0; p <= mask; ++p) {
-            const unsigned long long w = __ldg(table + s);
-            if (w == 0ull) return -1;
-            if (w == kst) return (int32_t)__ldg(vals + s);
-            s = (s + 1) & mask;
-        }
-        return -2;
+        if (empty) return -1;
+        g = (g + 1) & gmask;
+        load_group(table, g, w);
     }
+    return -2;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -151,7 +181,8 @@ __device__ __forceinline__ int32_t table_lookup(const unsigned long long *__rest
 template <bool KEY64>
 __global__ void __launch_bounds__(256)
 insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, int D,
-              unsigned long long *table, uint32_t *vals, uint64_t mask, int32_t *status) {
+              unsigned long long *table, uint32_t *vals, uint64_t gmask, uint32_t shift,
+              int32_t *status) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = __ldg(coords + i);
@@ -160,33 +191,42 @@ insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, i
             continue;
         }
         const uint64_t flat = ((((uint64_t)c.x * W + c.y) * H + c.z) * D) + c.w;
-        if (!table_insert<KEY64>(table, vals, mask, flat, (uint32_t)i, status))
+        if (!table_insert<KEY64>(table, vals, gmask, shift, flat, (uint32_t)i, status))
             raise_status(status, SPCONV_STATUS_TABLE_FULL);
     }
 }
 
 // ---------------------------------------------------------------------------------------
 // 2. Fused map + masks + order histogram (replaces torch::full + neighbor_map.cu:132-177).
-//    One warp per voxel: lane l handles offsets l, l+32, ...; a ballot yields each 32-bit
-//    word of the voxel's offset mask directly, and the V entries of the voxel are one
-//    contiguous store. Successive voxels of a block are adjacent, so the block writes one
-//    contiguous range of the map.
+//    One thread per voxel walks the voxel's V offsets in chunks of kMapChunk, with the
+//    chunk's table probes (one 32-byte group each) in flight together; the in-bounds test
+//    and key of each offset are one add against per-offset constants in shared memory. The
+//    thread builds the voxel's mask words in registers and stages its map row in shared
+//    memory, and the block then writes its voxels' rows as one contiguous, coalesced range.
+//    Blocks histogram their voxels by order key (popcount class, mask hash); the last
+//    block to finish turns the histogram into bucket offsets.
 // ---------------------------------------------------------------------------------------
+constexpr int kMapChunk = 8;
+constexpr int kMapStageMaxBytes = 96 * 1024;
+
 template <bool KEY64>
 __global__ void __launch_bounds__(kMapThreads)
 map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
-           int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW,
+           int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
            const unsigned long long *__restrict__ table, const uint32_t *__restrict__ vals,
-           uint64_t tmask, int32_t *__restrict__ nbr, uint32_t *__restrict__ masks,
+           uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr, uint32_t *__restrict__ masks,
            uint32_t *hist, uint32_t *cursor, uint32_t *done_counter, int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
     __shared__ uint32_t s_is_last;
     __shared__ uint32_t s_warp[kMapThreads / 32];
-    extern __shared__ int4 s_off[];                   // [V] (ox, oy, oz, unused)
+    extern __shared__ int4 s_off[];                                   // [V] (ox, oy, oz, 0)
+    long long *s_delta = reinterpret_cast<long long *>(s_off + V);   // [V] flat-key deltas
+    int32_t *s_stage = reinterpret_cast<int32_t *>(s_delta + V);     // [kMapThreads][vstride]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t i0 = (int64_t)blockIdx.x * kMapVoxels;
-    const int nvox = (M - i0) < (int64_t)kMapVoxels ? (int)(M - i0) : kMapVoxels;
+    const int64_t i0 = (int64_t)blockIdx.x * kMapThreads;
+    const int nvox = (M - i0) < (int64_t)kMapThreads ? (int)(M - i0) : kMapThreads;
+    const bool staged = vstride > 0;
 
     for (int v = tid; v < V; v += kMapThreads) {
         const int KhKd = Kh * Kd;
@@ -194,47 +234,87 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
         const int oy = ((v / Kd) % Kh) * Dh - (Kh / 2) * Dh;
         const int oz = (v % Kd) * Dd - (Kd / 2) * Dd;
         s_off[v] = make_int4(ox, oy, oz, 0);
+        // For in-bounds neighbours key(n) = key(c) + delta exactly.
+        s_delta[v] = ((long long)ox * H + oy) * D + oz;
     }
     for (int j = tid; j < kOrderBuckets; j += kMapThreads) s_hist[j] = 0u;
     __syncthreads();
 
+    const bool valid = tid < nvox;
+    const int64_t i = i0 + tid;
+    int4 c = make_int4(0, 0, 0, 0);
+    if (valid) c = __ldg(coords + i);
+    const unsigned long long base = ((((unsigned long long)(long long)c.x * W + c.y) * H + c.z) * D) + c.w;
     const int center = V / 2;
     bool wrapped = false;
-    for (int j = warp; j < nvox; j += kMapThreads / 32) {
-        const int64_t i = i0 + j;
-        const int4 c = __ldg(coords + i);
-        int32_t *out = nbr + i * (int64_t)V;
-        uint32_t *mrow = masks + i * (int64_t)MW;
-        uint32_t pc = 0, h = 0x9e3779b9u;
-        for (int vb = 0; vb < V; vb += 32) {
-            const int v = vb + lane;
-            int32_t value = -1;
-            if (v < V) {
-                if (v == center) {
-                    value = (int32_t)i;
-                } else {
-                    const int4 o = s_off[v];
-                    const int kx = c.y + o.x, ky = c.z + o.y, kz = c.w + o.z;
-                    if (kx >= 0 && kx < W && ky >= 0 && ky < H && kz >= 0 && kz < D) {
-                        const uint64_t flat = ((((uint64_t)(int64_t)c.x * W + kx) * H + ky) * D) + kz;
-                        value = table_lookup<KEY64>(table, vals, tmask, flat);
-                        if (value == -2) { wrapped = true; value = -1; }
+    uint32_t pc = 0, h = 0x9e3779b9u;
+    for (int vb = 0; vb < V; vb += 32) {
+        const int vend = min(vb + 32, V);
+        uint32_t bits = 0;
+        for (int v0 = vb; v0 < vend; v0 += kMapChunk) {
+            int32_t val[kMapChunk];
+            bool need[kMapChunk];
+            uint64_t flat[kMapChunk], grp[kMapChunk];
+            unsigned long long word[kMapChunk][kGroup];
+#pragma unroll
+            for (int k = 0; k < kMapChunk; ++k) {
+                const int v = v0 + k;
+                val[k] = -1;
+                need[k] = false;
+                if (valid && v < vend) {
+                    if (v == center) {
+                        val[k] = (int32_t)i;
+                    } else {
+                        const int4 o = s_off[v];
+                        if ((unsigned)(c.y + o.x) < (unsigned)W && (unsigned)(c.z + o.y) < (unsigned)H &&
+                            (unsigned)(c.w + o.z) < (unsigned)D) {
+                            flat[k] = base + (unsigned long long)s_delta[v];
+                            grp[k] = home_group<KEY64>(flat[k], gmask, shift);
+                            load_group(table, grp[k], word[k]);      // chunk probes in flight together
+                            need[k] = true;
+                        }
                     }
                 }
-                out[v] = value;
             }
-            const uint32_t bits = __ballot_sync(0xffffffffu, value >= 0);
-            if (lane == 0) mrow[vb >> 5] = bits;
-            pc += __popc(bits);
-            h = fmix32(h ^ bits);
+#pragma unroll
+            for (int k = 0; k < kMapChunk; ++k) {
+                const int v = v0 + k;
+                if (need[k]) {
+                    val[k] = table_resolve<KEY64>(table, vals, gmask, flat[k], grp[k], word[k]);
+                    if (val[k] == -2) { wrapped = true; val[k] = -1; }
+                }
+                if (valid && v < vend) {
+                    if (staged) s_stage[tid * vstride + v] = val[k];
+                    else nbr[i * (int64_t)V + v] = val[k];
+                    if (val[k] >= 0) bits |= 1u << (v - vb);
+                }
+            }
         }
-        if (lane == 0) {
-            const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-            atomicAdd(&s_hist[cls * 256u + (h & 255u)], 1u);
-        }
+        if (valid) masks[i * (int64_t)MW + (vb >> 5)] = bits;
+        pc += __popc(bits);
+        h = fmix32(h ^ bits);
     }
     if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
+    {
+        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+        const uint32_t key = cls * 256u + (h & 255u);
+        const uint32_t active = __ballot_sync(0xffffffffu, valid);
+        if (valid) aggregated_inc(s_hist, key, active);
+    }
     __syncthreads();
+
+    // The block's rows form one contiguous range of the map.
+    if (staged) {
+        int32_t *out = nbr + i0 * (int64_t)V;
+        const int total = nvox * V;
+        int il = tid / V, v = tid - il * V;
+        const int step_i = kMapThreads / V, step_v = kMapThreads - step_i * V;
+        for (int e = tid; e < total; e += kMapThreads) {
+            out[e] = s_stage[il * vstride + v];
+            v += step_v; il += step_i;
+            if (v >= V) { v -= V; ++il; }
+        }
+    }
     for (int b = tid; b < kOrderBuckets; b += kMapThreads)
         if (s_hist[b]) atomicAdd(hist + b, s_hist[b]);
 
@@ -245,7 +325,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     __syncthreads();
     if (!s_is_last) return;
     __threadfence();
-    constexpr int per = kOrderBuckets / kMapThreads;   // 16 buckets per thread
+    constexpr int per = kOrderBuckets / kMapThreads;
     uint32_t local[per];
     uint32_t sum = 0;
 #pragma unroll
@@ -312,10 +392,7 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, uint32_t *cu
 using namespace spconv;
 
 extern "C" int64_t spconv_hashmap_capacity(int64_t num_coords) {
-    int64_t need = num_coords > 0 ? 2 * num_coords : 0;
-    int64_t cap = 1024;
-    while (cap < need) cap <<= 1;
-    return cap;
+    return capacity_for(num_coords > 0 ? num_coords : 0);
 }
 
 extern "C" int spconv_mask_words(int kernel_volume) {
@@ -363,7 +440,9 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     uint32_t *hist = (uint32_t *)(ws + L.hist);
     uint32_t *cursor = (uint32_t *)(ws + L.cursor);
     uint32_t *counter = (uint32_t *)(ws + L.counter);
-    const uint64_t tmask = (uint64_t)L.cap - 1;
+    const uint64_t gmask = (uint64_t)(L.cap / kGroup) - 1;
+    uint32_t shift = 32;
+    for (int64_t c = L.cap / kGroup; c > 1; c >>= 1) --shift;   // 32 - log2(groups)
     const int MW = spconv_mask_words(V);
 
     stage_mark(SPCONV_STAGE_MEMSET, 0, stream);
@@ -374,23 +453,34 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     const int ins_grid = (int)(gi < 65535LL * 32 ? gi : 65535LL * 32);
     stage_mark(SPCONV_STAGE_INSERT, 0, stream);
     if (key64)
-        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, tmask, status);
+        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, gmask, shift, status);
     else
-        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, tmask, status);
+        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, gmask, shift, status);
     if (int rc = check_launch("insert_kernel")) return rc;
     stage_mark(SPCONV_STAGE_INSERT, 1, stream);
 
-    const int map_grid = (int)((M + kMapVoxels - 1) / kMapVoxels);
-    const size_t map_smem = (size_t)V * sizeof(int4);
+    const int map_grid = (int)((M + kMapThreads - 1) / kMapThreads);
+    // Rows are staged in shared memory (odd row stride: conflict-free) unless V is so large
+    // that the stage would not fit; then rows are stored directly.
+    int vstride = (V % 2 == 0) ? V + 1 : V;
+    if ((size_t)kMapThreads * vstride * 4 > (size_t)kMapStageMaxBytes) vstride = 0;
+    const size_t map_smem = (size_t)V * (sizeof(int4) + sizeof(long long)) +
+                            (size_t)kMapThreads * (size_t)vstride * sizeof(int32_t);
+    static bool map_attr_done[2] = {false, false};
+    if (map_smem > 48 * 1024 && !map_attr_done[key64 ? 1 : 0]) {
+        cudaFuncSetAttribute(key64 ? map_kernel<true> : map_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        map_attr_done[key64 ? 1 : 0] = true;
+    }
     stage_mark(SPCONV_STAGE_MAP, 0, stream);
     if (key64)
         map_kernel<true><<<map_grid, kMapThreads, map_smem, stream>>>(
-            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, table, vals, tmask,
-            neighbor_map, masks, hist, cursor, counter, status);
+            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, gmask,
+            shift, neighbor_map, masks, hist, cursor, counter, status);
     else
         map_kernel<false><<<map_grid, kMapThreads, map_smem, stream>>>(
-            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, table, vals, tmask,
-            neighbor_map, masks, hist, cursor, counter, status);
+            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, gmask,
+            shift, neighbor_map, masks, hist, cursor, counter, status);
     if (int rc = check_launch("map_kernel")) return rc;
     stage_mark(SPCONV_STAGE_MAP, 1, stream);
 
@@ -416,11 +506,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
 // ---------------------------------------------------------------------------------------
 namespace spconv {
 
-constexpr int64_t noalloc_capacity() {
-    int64_t cap = 1024;
-    while (cap < 2 * (int64_t)SPCONV_NOALLOC_MAX_COORDS) cap <<= 1;
-    return cap;
-}
+constexpr int64_t noalloc_capacity() { return capacity_for((int64_t)SPCONV_NOALLOC_MAX_COORDS); }
 constexpr int64_t align256c(int64_t x) { return (x + 255) & ~int64_t(255); }
 constexpr int64_t kNoAllocScratchBytes =
     align256c(noalloc_capacity() * 8) + align256c(noalloc_capacity() * 4) +

@@ -26,7 +26,7 @@ SPCONV_OK, SPCONV_ERR_ARG, SPCONV_ERR_CUDA, SPCONV_ERR_UNSUPPORTED = 0, 1, 2, 3
 STATUS_COORD_RANGE, STATUS_TABLE_FULL, STATUS_DUPLICATE, STATUS_WAIT_TIMEOUT = 1, 2, 4, 8
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 KERNEL_AUTO, KERNEL_SIMT, KERNEL_TCGEN05 = 0, 1, 2
-NOALLOC_MAX_COORDS = 524288   # SPCONV_NOALLOC_MAX_COORDS
+NOALLOC_MAX_COORDS = 262144   # SPCONV_NOALLOC_MAX_COORDS
 
 _c_i64, _c_int, _c_void_p = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
 
@@ -162,7 +162,12 @@ def _inspect(st: _DeviceStatus) -> None:
 
 
 def after_launch(device: torch.device) -> None:
-    """Queue the status read-back of this op; check at once if SPARSECONV_SYNC_CHECK=1."""
+    """Queue the status read-back of this op; check at once if SPARSECONV_SYNC_CHECK=1.
+
+    Skipped while the stream is being captured into a CUDA graph (call ``check_errors``
+    after replays instead)."""
+    if torch.cuda.is_current_stream_capturing():
+        return
     st = status_word(device)
     stream = torch.cuda.current_stream(device)
     st.host.copy_(st.word, non_blocking=True)
@@ -175,6 +180,8 @@ def after_launch(device: torch.device) -> None:
 
 def before_launch(device: torch.device) -> None:
     """Raise for an error found by an earlier op on this device, if its read-back landed."""
+    if torch.cuda.is_current_stream_capturing():
+        return
     st = status_word(device)
     if st.pending and st.event.query():
         _inspect(st)

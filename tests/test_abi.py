@@ -46,11 +46,14 @@ def test_abi_version(lib):
 
 def test_hashmap_capacity(lib):
     assert lib.spconv_hashmap_capacity(0) == 1024
-    assert lib.spconv_hashmap_capacity(512) == 1024
-    assert lib.spconv_hashmap_capacity(513) == 2048
-    for m in (1000, 168546, 2_000_000, 1_342_011):
+    assert lib.spconv_hashmap_capacity(256) == 1024
+    assert lib.spconv_hashmap_capacity(257) == 2048
+    for m in (1000, 168546, 2_000_000, 1_342_011):       # load <= 0.25 while the table is <= 64 MB
         cap = lib.spconv_hashmap_capacity(m)
-        assert cap >= 2 * m and cap & (cap - 1) == 0 and cap < 4 * m + 1024
+        assert cap >= 4 * m and cap & (cap - 1) == 0 and cap * 8 <= 64 << 20
+    for m in (3_000_000, 5_000_000):                      # larger tables: load <= 0.5
+        cap = lib.spconv_hashmap_capacity(m)
+        assert 2 * m <= cap < 4 * m and cap & (cap - 1) == 0
 
 
 def test_mask_words(lib):
