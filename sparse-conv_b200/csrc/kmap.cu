@@ -56,21 +56,33 @@ constexpr int64_t capacity_for(int64_t M) {
 struct WsLayout {
     int64_t cap = 0;
     bool key64 = false;
-    int64_t table = 0, vals = 0, hist = 0, cursor = 0, counter = 0, total = 0;
+    int64_t bitmap_words = 0;
+    int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, counter = 0, total = 0;
 };
+
+// Grids of at most 2^28 cells (a 32 MB bitmap) get an occupancy bitmap, one bit per cell,
+// that screens neighbour probes: a clear bit settles a probe with one cached 4-byte load.
+constexpr long double kBitmapMaxCells = 268435456.0L;
+static int64_t bitmap_words_for(int batch, int W, int H, int D) {
+    const long double vol = (long double)batch * W * H * D;
+    if (vol > kBitmapMaxCells) return 0;
+    return (int64_t)((vol + 31.0L) / 32.0L);
+}
 
 static bool volume_fits_32(int batch, int W, int H, int D) {
     const long double vol = (long double)batch * W * H * D;
     return vol < 4294967296.0L;
 }
 
-static WsLayout ws_layout(int64_t M, bool key64) {
+static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
     WsLayout L;
     L.cap = capacity_for(M);
     L.key64 = key64;
+    L.bitmap_words = key64 ? 0 : bitmap_words;
     int64_t off = 0;
     L.table = off; off += align256(L.cap * 8);
     if (key64) { L.vals = off; off += align256(L.cap * 4); }
+    if (L.bitmap_words) { L.bitmap = off; off += align256(L.bitmap_words * 4); }
     L.hist = off; off += align256(kOrderBuckets * 4);
     L.cursor = off; off += align256(kOrderBuckets * 4);
     L.counter = off; off += 256;
@@ -181,8 +193,8 @@ __device__ __forceinline__ int32_t table_resolve(const unsigned long long *__res
 template <bool KEY64>
 __global__ void __launch_bounds__(256)
 insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, int D,
-              unsigned long long *table, uint32_t *vals, uint64_t gmask, uint32_t shift,
-              int32_t *status) {
+              unsigned long long *table, uint32_t *vals, uint32_t *bitmap, uint64_t gmask,
+              uint32_t shift, int32_t *status) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = __ldg(coords + i);
@@ -191,6 +203,7 @@ insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, i
             continue;
         }
         const uint64_t flat = ((((uint64_t)c.x * W + c.y) * H + c.z) * D) + c.w;
+        if (bitmap) atomicOr(bitmap + (flat >> 5), 1u << (flat & 31));
         if (!table_insert<KEY64>(table, vals, gmask, shift, flat, (uint32_t)i, status))
             raise_status(status, SPCONV_STATUS_TABLE_FULL);
     }
@@ -209,12 +222,12 @@ insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, i
 constexpr int kMapChunk = 8;
 constexpr int kMapStageMaxBytes = 96 * 1024;
 
-template <bool KEY64>
+template <bool KEY64, bool BITMAP>
 __global__ void __launch_bounds__(kMapThreads)
 map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
            int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
            const unsigned long long *__restrict__ table, const uint32_t *__restrict__ vals,
-           uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr, uint32_t *__restrict__ masks,
+           const uint32_t *__restrict__ bitmap, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr, uint32_t *__restrict__ masks,
            uint32_t *hist, uint32_t *cursor, uint32_t *done_counter, int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
     __shared__ uint32_t s_is_last;
@@ -256,6 +269,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             bool need[kMapChunk];
             uint64_t flat[kMapChunk], grp[kMapChunk];
             unsigned long long word[kMapChunk][kGroup];
+            uint32_t occ[kMapChunk];
 #pragma unroll
             for (int k = 0; k < kMapChunk; ++k) {
                 const int v = v0 + k;
@@ -269,11 +283,18 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
                         if ((unsigned)(c.y + o.x) < (unsigned)W && (unsigned)(c.z + o.y) < (unsigned)H &&
                             (unsigned)(c.w + o.z) < (unsigned)D) {
                             flat[k] = base + (unsigned long long)s_delta[v];
-                            grp[k] = home_group<KEY64>(flat[k], gmask, shift);
-                            load_group(table, grp[k], word[k]);      // chunk probes in flight together
                             need[k] = true;
+                            if (BITMAP) occ[k] = __ldg(bitmap + (flat[k] >> 5));   // screens in flight together
                         }
                     }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kMapChunk; ++k) {
+                if (BITMAP && need[k]) need[k] = (occ[k] >> (flat[k] & 31)) & 1u;
+                if (need[k]) {
+                    grp[k] = home_group<KEY64>(flat[k], gmask, shift);
+                    load_group(table, grp[k], word[k]);              // chunk probes in flight together
                 }
             }
 #pragma unroll
@@ -345,6 +366,335 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
 }
 
 // ---------------------------------------------------------------------------------------
+// 2b. Map build for grids with an occupancy bitmap (32-bit keys). One thread per voxel
+//     walks the kernel column by column: a (dx, dy) column's z-offsets span at most 32
+//     cells, so one funnel-shifted pair of bitmap words screens all of them; only cells
+//     whose bit is set are probed in the hash table (the column's probes in flight
+//     together). Mask words are built in a register and flushed as v crosses a multiple
+//     of 32; map rows are staged in shared memory and written out coalesced.
+// ---------------------------------------------------------------------------------------
+constexpr int kMapBmMaxThreads = 256;
+constexpr int kColBatchMax = 8;          // Kd <= 8 (longer columns use map_kernel)
+
+__device__ __forceinline__ void block_hist_flush_and_scan(uint32_t *s_hist, uint32_t *s_warp,
+                                                          uint32_t *s_is_last, uint32_t *hist,
+                                                          uint32_t *cursor, uint32_t *done_counter) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+    for (int b = tid; b < kOrderBuckets; b += nthr)
+        if (s_hist[b]) atomicAdd(hist + b, s_hist[b]);
+    // The last block to finish converts the global histogram into bucket start offsets.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *s_is_last = (atomicAdd(done_counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+    __syncthreads();
+    if (!*s_is_last) return;
+    __threadfence();
+    const int per = kOrderBuckets / nthr;             // 16 (256 threads) or 32 (128 threads)
+    uint32_t sum = 0;
+    for (int k = 0; k < per; ++k) sum += __ldcg(hist + tid * per + k);
+    uint32_t incl = sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += n;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    uint32_t run = incl - sum;
+    for (int w = 0; w < warp; ++w) run += s_warp[w];
+    for (int k = 0; k < per; ++k) {
+        const uint32_t c = __ldcg(hist + tid * per + k);
+        cursor[tid * per + k] = run;
+        run += c;
+    }
+}
+
+template <int kColBatch>
+__global__ void __launch_bounds__(kMapBmMaxThreads, 3)
+map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
+              int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
+              const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
+              int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
+              uint32_t *__restrict__ masks, uint32_t *hist, uint32_t *cursor, uint32_t *done_counter,
+              int32_t *status) {
+    __shared__ uint32_t s_hist[kOrderBuckets];
+    __shared__ uint32_t s_is_last;
+    __shared__ uint32_t s_warp[kMapBmMaxThreads / 32];
+    extern __shared__ int32_t s_stage[];                       // [blockDim.x][vstride]
+
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * nthr;
+    const int nvox = (M - i0) < (int64_t)nthr ? (int)(M - i0) : nthr;
+    const bool staged = vstride > 0;
+    for (int j = tid; j < kOrderBuckets; j += nthr) s_hist[j] = 0u;
+    __syncthreads();
+
+    const bool valid = tid < nvox;
+    const int64_t i = i0 + tid;
+    int4 c = make_int4(0, 0, 0, 0);
+    if (valid) c = __ldg(coords + i);
+    const int64_t HD = (int64_t)H * D;
+    const int64_t key_c = (((int64_t)c.x * W + c.y) * H + c.z) * D + c.w;
+    const int rw = Kw / 2, rh = Kh / 2, rd = Kd / 2;
+    const int span = (Kd - 1) * Dd + 1;
+    const int center = V / 2;
+    bool wrapped = false;
+    uint32_t pc = 0, h = 0x9e3779b9u, cur_bits = 0;
+    int cur_w = 0, v = 0;
+    for (int cx = 0; cx < Kw; ++cx) {
+        const int ox = (cx - rw) * Dw;
+        const bool xin = (unsigned)(c.y + ox) < (unsigned)W;
+        for (int cy = 0; cy < Kh; ++cy) {
+            const int oy = (cy - rh) * Dh;
+            const bool yin = valid && xin && (unsigned)(c.z + oy) < (unsigned)H;
+            const int64_t col = key_c + ox * HD + (int64_t)oy * D;     // key of (x+ox, y+oy, z)
+            const int zlo = max(c.w - rd * Dd, 0);
+            const int64_t kbase = col + (zlo - c.w);
+            uint32_t win = 0;
+            if (yin && span <= 32) {
+                const int64_t wi = kbase >> 5;
+                const uint32_t lo = __ldg(bitmap + wi);
+                const uint32_t hi = __ldg(bitmap + (wi + 1 < bm_words ? wi + 1 : wi));
+                win = __funnelshift_r(lo, hi, (uint32_t)(kbase & 31));  // bits kbase .. kbase+31
+            }
+            int32_t val[kColBatch];
+            uint32_t key[kColBatch];
+            uint64_t grp[kColBatch];
+            bool need[kColBatch];
+            unsigned long long word[kColBatch][kGroup];
+#pragma unroll
+            for (int cz = 0; cz < kColBatch; ++cz) {
+                val[cz] = -1;
+                need[cz] = false;
+                if (cz < Kd) {
+                    const int oz = (cz - rd) * Dd;
+                    if (v + cz == center) {
+                        val[cz] = (int32_t)i;
+                    } else if (yin && (unsigned)(c.w + oz) < (unsigned)D) {
+                        const int64_t kn = col + oz;
+                        const bool present = span <= 32 ? ((win >> (uint32_t)(kn - kbase)) & 1u)
+                                                        : ((__ldg(bitmap + (kn >> 5)) >> (kn & 31)) & 1u);
+                        if (present) {
+                            key[cz] = (uint32_t)kn;
+                            grp[cz] = home32(key[cz], shift);
+                            load_group(table, grp[cz], word[cz]);    // the column's probes in flight together
+                            need[cz] = true;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int cz = 0; cz < kColBatch; ++cz) {
+                if (cz < Kd) {
+                    if (need[cz]) {
+                        val[cz] = table_resolve<false>(table, nullptr, gmask, key[cz], grp[cz], word[cz]);
+                        if (val[cz] == -2) { wrapped = true; val[cz] = -1; }
+                    }
+                    if ((v >> 5) != cur_w) {                         // mask word complete
+                        if (valid) masks[i * (int64_t)MW + cur_w] = cur_bits;
+                        pc += __popc(cur_bits);
+                        h = fmix32(h ^ cur_bits);
+                        cur_w = v >> 5;
+                        cur_bits = 0;
+                    }
+                    if (valid) {
+                        if (staged) s_stage[tid * vstride + v] = val[cz];
+                        else nbr[i * (int64_t)V + v] = val[cz];
+                    }
+                    if (val[cz] >= 0) cur_bits |= 1u << (v & 31);
+                    ++v;
+                }
+            }
+        }
+    }
+    if (valid) masks[i * (int64_t)MW + cur_w] = cur_bits;
+    pc += __popc(cur_bits);
+    h = fmix32(h ^ cur_bits);
+    if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
+    {
+        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t active = __ballot_sync(0xffffffffu, valid);
+        if (valid) aggregated_inc(s_hist, k, active);
+    }
+    __syncthreads();
+
+    // The block's rows form one contiguous range of the map.
+    if (staged) {
+        int32_t *out = nbr + i0 * (int64_t)V;
+        const int total = nvox * V;
+        if (vstride == V && ((uintptr_t)out & 15u) == 0) {
+            const int n4 = total >> 2;
+            const int4 *src = reinterpret_cast<const int4 *>(s_stage);
+            int4 *dst = reinterpret_cast<int4 *>(out);
+            for (int e = tid; e < n4; e += nthr) dst[e] = src[e];
+            for (int e = (n4 << 2) + tid; e < total; e += nthr) out[e] = s_stage[e];
+        } else {
+            int il = tid / V, vv = tid - il * V;
+            const int step_i = nthr / V, step_v = nthr - step_i * V;
+            for (int e = tid; e < total; e += nthr) {
+                out[e] = s_stage[il * vstride + vv];
+                vv += step_v; il += step_i;
+                if (vv >= V) { vv -= V; ++il; }
+            }
+        }
+    }
+    block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+}
+
+// ---------------------------------------------------------------------------------------
+// 2c. Map build for 3x3x3 kernels (any dilation). Phase 1 forms a 27-bit candidate mask
+//     per voxel: six per-voxel in-bounds flags and, with a bitmap, one funnel-shifted window
+//     per (dx, dy) column (all 18 window loads issued up front). Phase 2 probes the hash
+//     table only for candidate offsets, four in flight at a time. The block's map rows are
+//     pre-filled with -1 in shared memory, so only found neighbours and the centre are
+//     stored before the rows are written out coalesced.
+// ---------------------------------------------------------------------------------------
+constexpr int kMapK3Threads = 256;
+constexpr int kK3Batch = 4;
+
+template <bool BITMAP>
+__global__ void __launch_bounds__(kMapK3Threads, 3)
+map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
+              const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
+              int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
+              uint32_t *__restrict__ masks, uint32_t *hist, uint32_t *cursor, uint32_t *done_counter,
+              int32_t *status) {
+    constexpr int V = 27;
+    __shared__ uint32_t s_hist[kOrderBuckets];
+    __shared__ uint32_t s_is_last;
+    __shared__ uint32_t s_warp[kMapK3Threads / 32];
+    __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
+
+    const int tid = threadIdx.x;
+    const int64_t i0 = (int64_t)blockIdx.x * kMapK3Threads;
+    const int nvox = (M - i0) < (int64_t)kMapK3Threads ? (int)(M - i0) : kMapK3Threads;
+    for (int j = tid; j < kOrderBuckets; j += kMapK3Threads) s_hist[j] = 0u;
+    {
+        int4 *st4 = reinterpret_cast<int4 *>(s_stage);
+        for (int j = tid; j < kMapK3Threads * V / 4; j += kMapK3Threads) st4[j] = make_int4(-1, -1, -1, -1);
+    }
+
+    const bool valid = tid < nvox;
+    const int64_t i = i0 + tid;
+    int4 c = make_int4(0, 0, 0, 0);
+    if (valid) c = __ldg(coords + i);
+    const int64_t HD = (int64_t)H * D;
+    const int64_t key_c = (((int64_t)c.x * W + c.y) * H + c.z) * D + c.w;
+    const int64_t sx = (int64_t)Dw * HD, sy = (int64_t)Dh * D;
+    const bool in_x[3] = {c.y - Dw >= 0, true, c.y + Dw < W};
+    const bool in_y[3] = {c.z - Dh >= 0, true, c.z + Dh < H};
+    const bool in_z[3] = {c.w - Dd >= 0, true, c.w + Dd < D};
+    const uint32_t zbits = (in_z[0] ? 1u : 0u) | 2u | (in_z[2] ? 4u : 0u);
+
+    // Phase 1: candidate offsets.
+    uint32_t cand = 0;
+    if (valid) {
+        if (BITMAP && 2 * Dd + 1 <= 32) {
+            uint32_t lo[9], hi[9];
+            const int zoff = in_z[0] ? Dd : 0;                 // window starts at the lowest in-range cell
+#pragma unroll
+            for (int q = 0; q < 9; ++q) {
+                const int dx = q / 3, dy = q % 3;
+                lo[q] = hi[q] = 0;
+                if (in_x[dx] && in_y[dy]) {
+                    const int64_t kb = key_c + (dx - 1) * sx + (dy - 1) * sy - zoff;
+                    const int64_t wi = kb >> 5;
+                    lo[q] = __ldg(bitmap + wi);
+                    hi[q] = __ldg(bitmap + (wi + 1 < bm_words ? wi + 1 : wi));
+                }
+            }
+            const int64_t k0 = key_c - zoff;                   // same low-bit phase for every column
+#pragma unroll
+            for (int q = 0; q < 9; ++q) {
+                const int dx = q / 3, dy = q % 3;
+                if (in_x[dx] && in_y[dy]) {
+                    const int64_t kb = k0 + (dx - 1) * sx + (dy - 1) * sy;
+                    const uint32_t win = __funnelshift_r(lo[q], hi[q], (uint32_t)(kb & 31));
+                    const uint32_t b0 = in_z[0] ? (win & 1u) : 0u;                 // z - Dd
+                    const uint32_t b1 = (win >> zoff) & 1u;                          // z
+                    const uint32_t b2 = in_z[2] ? ((win >> (zoff + Dd)) & 1u) : 0u;  // z + Dd
+                    cand |= (b0 | (b1 << 1) | (b2 << 2)) << (3 * q);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 9; ++q)
+                if (in_x[q / 3] && in_y[q % 3]) cand |= zbits << (3 * q);
+            if (BITMAP) {                                       // wide dilation: one load per cell
+                uint32_t keep = 0;
+                for (uint32_t m = cand; m; m &= m - 1) {
+                    const int v = __ffs(m) - 1;
+                    const int64_t kn = key_c + (v / 9 - 1) * sx + ((v / 3) % 3 - 1) * sy + (int64_t)(v % 3 - 1) * Dd;
+                    if ((__ldg(bitmap + (kn >> 5)) >> (kn & 31)) & 1u) keep |= 1u << v;
+                }
+                cand = keep;
+            }
+        }
+    }
+    cand &= ~(1u << (V / 2));                                   // the centre is the voxel itself
+
+    __syncthreads();                                            // hist zeroed, stage pre-filled
+    uint32_t bits = valid ? (1u << (V / 2)) : 0u;
+    if (valid) s_stage[tid * V + V / 2] = (int32_t)i;
+
+    // Phase 2: probe candidate offsets, kK3Batch in flight.
+    bool wrapped = false;
+    while (cand) {
+        int vv[kK3Batch];
+        uint32_t key[kK3Batch];
+        uint64_t grp[kK3Batch];
+        unsigned long long word[kK3Batch][kGroup];
+#pragma unroll
+        for (int b = 0; b < kK3Batch; ++b) {
+            vv[b] = -1;
+            if (cand) {
+                const int v = __ffs(cand) - 1;
+                cand &= cand - 1;
+                vv[b] = v;
+                const int64_t kn = key_c + (v / 9 - 1) * sx + ((v / 3) % 3 - 1) * sy + (int64_t)(v % 3 - 1) * Dd;
+                key[b] = (uint32_t)kn;
+                grp[b] = home32(key[b], shift);
+                load_group(table, grp[b], word[b]);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < kK3Batch; ++b) {
+            if (vv[b] >= 0) {
+                int32_t r = table_resolve<false>(table, nullptr, gmask, key[b], grp[b], word[b]);
+                if (r == -2) { wrapped = true; r = -1; }
+                if (r >= 0) {
+                    s_stage[tid * V + vv[b]] = r;
+                    bits |= 1u << vv[b];
+                }
+            }
+        }
+    }
+    if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
+    if (valid) masks[i] = bits;
+    {
+        const uint32_t pc = __popc(bits);
+        const uint32_t h = fmix32(0x9e3779b9u ^ bits);
+        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t active = __ballot_sync(0xffffffffu, valid);
+        if (valid) aggregated_inc(s_hist, k, active);
+    }
+    __syncthreads();
+    {
+        // The block's rows form one contiguous range of the map (16-byte aligned: i0 % 256 == 0).
+        int32_t *out = nbr + i0 * (int64_t)V;
+        const int total = nvox * V;
+        const int n4 = total >> 2;
+        const int4 *src = reinterpret_cast<const int4 *>(s_stage);
+        int4 *dst = reinterpret_cast<int4 *>(out);
+        for (int e = tid; e < n4; e += kMapK3Threads) dst[e] = src[e];
+        for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
+    }
+    block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+}
+
+// ---------------------------------------------------------------------------------------
 // 3. Counting-sort scatter of voxel ids by order key.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kOrderThreads)
@@ -401,7 +751,7 @@ extern "C" int spconv_mask_words(int kernel_volume) {
 
 extern "C" int64_t spconv_neighbor_map_workspace_bytes(int64_t num_coords, int batch, int W, int H, int D) {
     if (num_coords < 0) return -1;
-    return ws_layout(num_coords, !volume_fits_32(batch, W, H, D)).total;
+    return ws_layout(num_coords, !volume_fits_32(batch, W, H, D), bitmap_words_for(batch, W, H, D)).total;
 }
 
 extern "C" int spconv_build_submanifold_neighbor_map(
@@ -430,13 +780,16 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     SPCONV_REQUIRE(((uintptr_t)coords & 15u) == 0, SPCONV_ERR_ARG, "coords must be 16-byte aligned");
     SPCONV_REQUIRE(((uintptr_t)workspace & 255u) == 0, SPCONV_ERR_ARG, "workspace must be 256-byte aligned");
     const bool key64 = !volume_fits_32(batch, W, H, D);
-    const WsLayout L = ws_layout(M, key64);
+    // The occupancy bitmap is used when the workspace has room for it.
+    WsLayout L = ws_layout(M, key64, bitmap_words_for(batch, W, H, D));
+    if (L.bitmap_words && workspace_bytes < L.total) L = ws_layout(M, key64, 0);
     SPCONV_REQUIRE(workspace_bytes >= L.total, SPCONV_ERR_ARG,
                    "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)L.total);
     cudaStream_t stream = (cudaStream_t)stream_ptr;
     char *ws = (char *)workspace;
     unsigned long long *table = (unsigned long long *)(ws + L.table);
     uint32_t *vals = key64 ? (uint32_t *)(ws + L.vals) : nullptr;
+    uint32_t *bitmap = L.bitmap_words ? (uint32_t *)(ws + L.bitmap) : nullptr;
     uint32_t *hist = (uint32_t *)(ws + L.hist);
     uint32_t *cursor = (uint32_t *)(ws + L.cursor);
     uint32_t *counter = (uint32_t *)(ws + L.counter);
@@ -453,34 +806,56 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     const int ins_grid = (int)(gi < 65535LL * 32 ? gi : 65535LL * 32);
     stage_mark(SPCONV_STAGE_INSERT, 0, stream);
     if (key64)
-        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, gmask, shift, status);
+        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status);
     else
-        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, gmask, shift, status);
+        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status);
     if (int rc = check_launch("insert_kernel")) return rc;
     stage_mark(SPCONV_STAGE_INSERT, 1, stream);
 
-    const int map_grid = (int)((M + kMapThreads - 1) / kMapThreads);
-    // Rows are staged in shared memory (odd row stride: conflict-free) unless V is so large
-    // that the stage would not fit; then rows are stored directly.
-    int vstride = (V % 2 == 0) ? V + 1 : V;
-    if ((size_t)kMapThreads * vstride * 4 > (size_t)kMapStageMaxBytes) vstride = 0;
-    const size_t map_smem = (size_t)V * (sizeof(int4) + sizeof(long long)) +
-                            (size_t)kMapThreads * (size_t)vstride * sizeof(int32_t);
-    static bool map_attr_done[2] = {false, false};
-    if (map_smem > 48 * 1024 && !map_attr_done[key64 ? 1 : 0]) {
-        cudaFuncSetAttribute(key64 ? map_kernel<true> : map_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        map_attr_done[key64 ? 1 : 0] = true;
+    if (!key64 && Kw == 3 && Kh == 3 && Kd == 3) {
+        auto k3_fn = bitmap ? map_kernel_k3<true> : map_kernel_k3<false>;
+        const int grid = (int)((M + kMapK3Threads - 1) / kMapK3Threads);
+        stage_mark(SPCONV_STAGE_MAP, 0, stream);
+        k3_fn<<<grid, kMapK3Threads, 0, stream>>>(
+            (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, table, bitmap, L.bitmap_words, gmask, shift,
+            neighbor_map, masks, hist, cursor, counter, status);
+    } else if (bitmap && Kd <= kColBatchMax) {
+        // 256 voxels per block while their staged rows fit in 64 KB, else 128.
+        const int nthr = ((size_t)kMapBmMaxThreads * (V | 1) * 4 <= 64 * 1024) ? kMapBmMaxThreads : 128;
+        int vstride = (V % 2 == 0) ? V + 1 : V;
+        if ((size_t)nthr * vstride * 4 > (size_t)kMapStageMaxBytes) vstride = 0;
+        const size_t smem = (size_t)nthr * (size_t)vstride * sizeof(int32_t);
+        auto bm_fn = Kd <= 4 ? map_kernel_bm<4> : map_kernel_bm<kColBatchMax>;
+        static bool bm_attr_done[2] = {false, false};
+        if (!bm_attr_done[Kd <= 4 ? 0 : 1]) {
+            cudaFuncSetAttribute(bm_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+            bm_attr_done[Kd <= 4 ? 0 : 1] = true;
+        }
+        const int grid = (int)((M + nthr - 1) / nthr);
+        stage_mark(SPCONV_STAGE_MAP, 0, stream);
+        bm_fn<<<grid, nthr, smem, stream>>>(
+            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, bitmap,
+            L.bitmap_words, gmask, shift, neighbor_map, masks, hist, cursor, counter, status);
+    } else {
+        const int map_grid = (int)((M + kMapThreads - 1) / kMapThreads);
+        // Rows are staged in shared memory (odd row stride: conflict-free) unless V is so
+        // large that the stage would not fit; then rows are stored directly.
+        int vstride = (V % 2 == 0) ? V + 1 : V;
+        if ((size_t)kMapThreads * vstride * 4 > (size_t)kMapStageMaxBytes) vstride = 0;
+        const size_t map_smem = (size_t)V * (sizeof(int4) + sizeof(long long)) +
+                                (size_t)kMapThreads * (size_t)vstride * sizeof(int32_t);
+        auto map_fn = key64 ? map_kernel<true, false> : (bitmap ? map_kernel<false, true> : map_kernel<false, false>);
+        static bool map_attr_done[3] = {false, false, false};
+        const int variant = key64 ? 0 : (bitmap ? 2 : 1);
+        if (map_smem > 48 * 1024 && !map_attr_done[variant]) {
+            cudaFuncSetAttribute(map_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+            map_attr_done[variant] = true;
+        }
+        stage_mark(SPCONV_STAGE_MAP, 0, stream);
+        map_fn<<<map_grid, kMapThreads, map_smem, stream>>>(
+            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, bitmap,
+            gmask, shift, neighbor_map, masks, hist, cursor, counter, status);
     }
-    stage_mark(SPCONV_STAGE_MAP, 0, stream);
-    if (key64)
-        map_kernel<true><<<map_grid, kMapThreads, map_smem, stream>>>(
-            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, gmask,
-            shift, neighbor_map, masks, hist, cursor, counter, status);
-    else
-        map_kernel<false><<<map_grid, kMapThreads, map_smem, stream>>>(
-            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, gmask,
-            shift, neighbor_map, masks, hist, cursor, counter, status);
     if (int rc = check_launch("map_kernel")) return rc;
     stage_mark(SPCONV_STAGE_MAP, 1, stream);
 

@@ -110,3 +110,29 @@ def test_non_default_stream():
     s.synchronize()
     np.testing.assert_array_equal(nbr.cpu().numpy().view(np.uint32),
                                   oracle.neighbor_map(coords, shape, ks, dil))
+
+
+@pytest.mark.parametrize("name", ["rand3", "rand5", "aniso", "dense3"])
+def test_hash_only_path_matches_bitmap_path(name):
+    """Grids of <= 2^28 cells screen probes with an occupancy bitmap when the workspace has
+    room for it; with a workspace too small for the bitmap the build probes the hash table
+    alone. Both must give the oracle's map."""
+    coords, shape, ks, dil = gpu_cases.small_cases()[name]
+    N, _C, W, H, D = shape
+    lib = _native.load_library()
+    c = torch.from_numpy(coords).cuda()
+    M, V = coords.shape[0], ks[0] * ks[1] * ks[2]
+    with_bitmap = _native.workspace_bytes(M, N, W, H, D)
+    bitmap_bytes = ((((N * W * H * D) + 31) // 32) * 4 + 255) // 256 * 256
+    ws = torch.empty((with_bitmap - bitmap_bytes,), dtype=torch.uint8, device="cuda")
+    nbr = torch.empty((M, V), dtype=torch.int32, device="cuda")
+    masks = torch.empty((M, (V + 31) // 32), dtype=torch.int32, device="cuda")
+    order = torch.empty((M,), dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = lib.spconv_build_submanifold_neighbor_map(
+        c.data_ptr(), M, N, W, H, D, *ks, *dil, ws.data_ptr(), ws.numel(), nbr.data_ptr(),
+        masks.data_ptr(), order.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.spconv_last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    np.testing.assert_array_equal(nbr.cpu().numpy().view(np.uint32), oracle.neighbor_map(coords, shape, ks, dil))
