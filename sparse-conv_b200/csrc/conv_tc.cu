@@ -23,17 +23,30 @@ namespace spconv {
 
 constexpr int kTcThreads = 128;
 constexpr int kTileM = 128;
-constexpr int kTcStages = 3;
+constexpr int kMaskPrefetchWords = 4;      // next-tile mask words held in registers (V <= 128)
 
 template <int CI, int CO>
 struct TcCfg {
     static constexpr int kABytes = kTileM * CI * 2;
     static constexpr int kBBytes = CO * CI * 2;
+    // Gathers run kAhead = kStages - 2 offsets ahead of the MMA: a refilled stage was last
+    // read by the MMA two offsets back, so its completion is off the critical path.
+    // Small stages: five (three ahead); mid-size: four; Ci = Co = 128: three (one ahead).
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = kStageBytes <= 8 * 1024 ? 6 : (kStageBytes <= 16 * 1024 ? 5 : (kStageBytes <= 32 * 1024 ? 4 : 3));
+    static constexpr int kAhead = kStages - 2;
     static constexpr int kTmemCols = CO < 32 ? 32 : CO;
     static constexpr int kAuxBytes = 256;
-    static constexpr int kSmemBytes = kTcStages * (kABytes + kBBytes) + kAuxBytes + 128;
+    static constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + kAuxBytes + 128;
     static constexpr int kMaxCtasByTmem = 512 / kTmemCols;
 };
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait_upto(int pending) {
+    // wait until at most `pending` (<= N) groups are outstanding
+    if (pending >= N) { cp_async_wait<N>(); return; }
+    if constexpr (N > 0) cp_async_wait_upto<N - 1>(pending);
+}
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
@@ -60,15 +73,15 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     uint8_t *sA = base;
-    uint8_t *sB = base + kTcStages * Cfg::kABytes;
-    uint8_t *aux = sB + kTcStages * Cfg::kBBytes;
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(aux);               // [kTcStages]
+    uint8_t *sB = base + Cfg::kStages * Cfg::kABytes;
+    uint8_t *aux = sB + Cfg::kStages * Cfg::kBBytes;
+    uint64_t *mbar = reinterpret_cast<uint64_t *>(aux);               // [Cfg::kStages]
     uint32_t *s_tmem = reinterpret_cast<uint32_t *>(aux + 64);
     uint32_t *s_maskw = reinterpret_cast<uint32_t *>(aux + 128);      // [<= 32]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < kTcStages; ++s) mbar_init(smem_u32(&mbar[s]), 1);
+        for (int s = 0; s < Cfg::kStages; ++s) mbar_init(smem_u32(&mbar[s]), 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 0) {
@@ -84,26 +97,52 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
 
     uint32_t it = 0;          // stage uses issued by this CTA so far
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    // Tiles are taken from the end of the voxel order first: voxels with the most neighbours
+    // sort last, and their tiles (the most active offsets) then start earliest.
+    const int G = gridDim.x;
+    const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    auto row_of = [&](int k) -> int32_t {
+        const int tile = num_tiles - 1 - ((int)blockIdx.x + k * G);
         const int64_t r = (int64_t)tile * kTileM + tid;
-        int32_t row = -1;
-        if (r < M) row = order ? __ldg(order + r) : (int32_t)r;
-        if (row >= M) row = -1;                   // an order entry outside the table is ignored
+        int32_t rr = -1;
+        if (r < M) rr = order ? __ldg(order + r) : (int32_t)r;
+        return rr >= M ? -1 : rr;                 // an order entry outside the table is ignored
+    };
+    auto mask_word = [&](int32_t rr, int w) -> uint32_t {
+        if (rr < 0) return 0u;
+        return masks ? __ldg(masks + (int64_t)rr * MW + w) : full_mask_word(w, V);
+    };
+    // Row and mask words of the next tile are loaded while the current tile runs.
+    int32_t row_next = my_tiles > 0 ? row_of(0) : -1;
+    uint32_t mk_next[kMaskPrefetchWords];
+#pragma unroll
+    for (int w = 0; w < kMaskPrefetchWords; ++w) mk_next[w] = w < MW ? mask_word(row_next, w) : 0u;
+
+    for (int k = 0; k < my_tiles; ++k) {
+        const int32_t row = row_next;
+        uint32_t mk[kMaskPrefetchWords];
+#pragma unroll
+        for (int w = 0; w < kMaskPrefetchWords; ++w) mk[w] = mk_next[w];
+        if (k + 1 < my_tiles) row_next = row_of(k + 1);
 
         __syncthreads();                          // previous tile done with s_maskw and TMEM
         if (tid < MW) s_maskw[tid] = 0u;
         __syncthreads();
         for (int w = 0; w < MW; ++w) {
             uint32_t m = 0;
-            if (row >= 0) m = masks ? __ldg(masks + (int64_t)row * MW + w) : full_mask_word(w, V);
+            if (MW <= kMaskPrefetchWords) {
+#pragma unroll
+                for (int q = 0; q < kMaskPrefetchWords; ++q) if (q == w) m = mk[q];
+            } else {
+                m = mask_word(row, w);
+            }
             m = __reduce_or_sync(0xffffffffu, m) & full_mask_word(w, V);
             if (lane == 0 && m) atomicOr(&s_maskw[w], m);
         }
         __syncthreads();
 
-        // Active offsets are consumed in ascending v. The gather of offset j+1 is issued
-        // before waiting for offset j's data, so two gathers are in flight per thread while
-        // the tensor core works on the previous offset.
+        // Active offsets are consumed in ascending v. Gathers run kAhead offsets ahead of the
+        // MMA, so several are in flight per thread while the tensor core works.
         const int32_t *nrow = nbr + (int64_t)(row < 0 ? 0 : row) * V;
         int nact = 0;
         for (int w = 0; w < MW; ++w) nact += __popc(s_maskw[w]);
@@ -115,8 +154,8 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
             const int v = iw * 32 + __ffs(im) - 1;
             im &= im - 1u;
             const uint32_t slot = it0 + (uint32_t)jj;
-            const int s = (int)(slot % kTcStages);
-            const uint32_t use = slot / kTcStages;
+            const int s = (int)(slot % Cfg::kStages);
+            const uint32_t use = slot / Cfg::kStages;
             if (use > 0 && !mbar_wait_bounded(smem_u32(&mbar[s]), (use - 1u) & 1u)) ok = false;
             int32_t n = row >= 0 ? __ldg(nrow + v) : -1;
             if (n >= M) n = -1;                   // rows outside the feature table read as missing
@@ -134,27 +173,24 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
             }
             cp_async_commit();
         };
-        if (nact > 0) issue(0);
+        int issued = 0;
+        while (issued < nact && issued < Cfg::kAhead) issue(issued++);
         int j = 0;
         for (; j < nact; ++j) {
-            if (j + 1 < nact) {
-                issue(j + 1);
-                cp_async_wait<1>();               // offset j's group has landed
-            } else {
-                cp_async_wait<0>();
-            }
+            if (issued < nact) issue(issued++);
+            cp_async_wait_upto<Cfg::kAhead>(issued - j - 1);   // offset j's group has landed
             fence_proxy_async_smem();
             if (!__syncthreads_and(ok)) { ok = false; break; }
-            const int s = (int)((it0 + (uint32_t)j) % kTcStages);
+            const int s = (int)((it0 + (uint32_t)j) % Cfg::kStages);
             if (tid == 0) {
                 tc_fence_after();
                 const uint32_t a_st = a_stage0 + s * Cfg::kABytes;
                 const uint32_t b_st = b_stage0 + s * Cfg::kBBytes;
 #pragma unroll
-                for (int k = 0; k < CI / 16; ++k) {
-                    const uint64_t ad = smem_desc_kmajor_noswizzle(a_st + k * 2 * (kTileM * 16), kTileM * 16, 128);
-                    const uint64_t bd = smem_desc_kmajor_noswizzle(b_st + k * 2 * (CO * 16), CO * 16, 128);
-                    tc_mma_f16(tmem, ad, bd, idesc, (j | k) != 0 ? 1u : 0u);
+                for (int kk = 0; kk < CI / 16; ++kk) {
+                    const uint64_t ad = smem_desc_kmajor_noswizzle(a_st + kk * 2 * (kTileM * 16), kTileM * 16, 128);
+                    const uint64_t bd = smem_desc_kmajor_noswizzle(b_st + kk * 2 * (CO * 16), CO * 16, 128);
+                    tc_mma_f16(tmem, ad, bd, idesc, (j | kk) != 0 ? 1u : 0u);
                 }
                 tc_commit(smem_u32(&mbar[s]));
             }
@@ -164,9 +200,13 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
             cp_async_wait<0>();
             break;
         }
+        // The next tile's mask words (its row load has landed by now).
+#pragma unroll
+        for (int w = 0; w < kMaskPrefetchWords; ++w)
+            mk_next[w] = (k + 1 < my_tiles && w < MW && MW <= kMaskPrefetchWords) ? mask_word(row_next, w) : 0u;
         if (j > 0) {
             const uint32_t last = it - 1u;
-            if (!mbar_wait_bounded(smem_u32(&mbar[last % kTcStages]), (last / kTcStages) & 1u)) ok = false;
+            if (!mbar_wait_bounded(smem_u32(&mbar[last % Cfg::kStages]), (last / Cfg::kStages) & 1u)) ok = false;
         }
         if (!__syncthreads_and(ok)) { ok = false; break; }
         tc_fence_after();
@@ -209,7 +249,7 @@ conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
             raise_status(status, SPCONV_STATUS_WAIT_TIMEOUT);
             if (it > 0) {
                 const uint32_t last = it - 1u;
-                mbar_wait_bounded(smem_u32(&mbar[last % kTcStages]), (last / kTcStages) & 1u);
+                mbar_wait_bounded(smem_u32(&mbar[last % Cfg::kStages]), (last / Cfg::kStages) & 1u);
             }
         }
     }
