@@ -78,6 +78,9 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint3
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n"
                  :: "r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" :: "r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
@@ -106,6 +109,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
         : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
     return ok != 0;
 }
+// Non-blocking test: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}\n"
+        : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+    return ok != 0;
+}
 // Bounded wait for the phase with the given parity to complete. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t addr, uint32_t parity) {
     if (mbar_try_wait(addr, parity)) return true;
@@ -120,10 +133,34 @@ __device__ __forceinline__ void mbar_arrive(uint32_t addr) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n"
                  :: "r"(addr) : "memory");
 }
-// Arrive on the mbarrier once every cp.async issued so far by this thread has landed; the
-// arrival counts toward the barrier's expected count (.noinc).
-__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t addr) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" :: "r"(addr) : "memory");
+// Arrive and add `bytes` to the phase's expected transaction count (TMA completions).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t addr, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n"
+                 :: "r"(addr), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor), completion on an mbarrier of this CTA. No multicast.
+// ---------------------------------------------------------------------------------------
+// Four rows (y0..y3) of a 2-D tensor, columns [x, x + box width), into consecutive box rows at
+// `dst`. Rows outside the tensor (negative or >= its height) are filled with zeros.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void *tmap, int x, int y0, int y1,
+                                            int y2, int y3, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n"
+        :: "r"(dst), "l"(tmap), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(mbar)
+        : "memory");
+}
+// One box of a 2-D tensor at (x, y).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int x, int y, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];\n"
+        :: "r"(dst), "l"(tmap), "r"(x), "r"(y), "r"(mbar) : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
+    asm volatile("prefetch.tensormap [%0];\n" :: "l"(tmap) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;\n" ::: "memory");
@@ -185,6 +222,14 @@ __device__ __forceinline__ void tc_commit(uint32_t mbar_addr) {
 __device__ __forceinline__ void tc_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
+// 32 lanes x 32 bits, 8 consecutive columns: thread l of the warp gets lane (base+l).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+          "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr) : "memory");
+}
 // 32 lanes x 32 bits, 16 consecutive columns: thread l of the warp gets lane (base+l).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
@@ -207,6 +252,23 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor_noswizzle(uint32_t saddr, u
     d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
     d |= (uint64_t)1 << 46;
+    return d;
+}
+
+// Shared-memory matrix descriptor, K-major with a 32/64/128-byte swizzle (the layout a TMA
+// load with the same swizzle writes): rows of `row_bytes` (= the swizzle width) one after
+// another, 8-row groups 8 * row_bytes apart, and within each row the 16-byte chunk index
+// XOR-ed with address bits 7 and up (bits [4, 4+log2(row_bytes/16)) ^= bits [7, ...)).
+// The tile must start on a multiple of 8 * row_bytes; a K step of 16 elements inside the
+// row advances `saddr` by 32 bytes.
+__device__ __forceinline__ uint64_t smem_desc_kmajor_swizzled(uint32_t saddr, uint32_t row_bytes) {
+    const uint64_t layout = row_bytes == 128 ? 2u : (row_bytes == 64 ? 4u : 6u);
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;                                   // leading offset: unused, 1
+    d |= (uint64_t)(((8u * row_bytes) >> 4) & 0x3FFFu) << 32; // 8-row group stride
+    d |= (uint64_t)1 << 46;                                   // descriptor version
+    d |= layout << 61;
     return d;
 }
 

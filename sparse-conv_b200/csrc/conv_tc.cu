@@ -1,49 +1,92 @@
 // tcgen05 / TMEM implicit-GEMM submanifold convolution for sm_100a (fp16 / bf16 in,
 // fp32 accumulate). Replaces the reference's Triton kernel (implicit_gemm.py:8-57), which
-// runs 32x32x16 tiles over every one of the V*ceil(Ci/16) K-steps and reloads the
-// neighbour index column per step.
+// runs 32x32x16 tiles over every one of the V*ceil(Ci/16) K-steps and reloads the neighbour
+// index column per step.
 //
-// Structure (one CTA = 4 warps = 128 threads, persistent over 128-row tiles):
-//   * a tile is 128 consecutive entries of the voxel order produced by the map build, so
-//     rows of a tile share most of their offset masks; the OR of the tile's masks selects
-//     the offsets the tile needs (every offset absent from all 128 rows is skipped);
-//   * for each active offset v, thread t gathers feature row nbr[row_t, v] (zero-filled by
-//     cp.async when missing) into the A stage and the CTA loads W[:, v, :] into the B
-//     stage, both K-major in the no-swizzle core-matrix layout (8 rows x 16 bytes);
-//   * one thread issues Ci/16 tcgen05.mma (M=128, N=Co, K=16) accumulating into TMEM and
-//     commits to the stage's mbarrier, so the next offset's gather overlaps the MMAs;
-//   * epilogue: tcgen05.ld of each warp's 32 TMEM lanes, + bias, one rounding to the
-//     output dtype, and a single store of each output row (no atomics).
-// Every mbarrier wait is bounded; on timeout the CTA raises SPCONV_STATUS_WAIT_TIMEOUT,
-// waits (bounded) for its last MMAs, frees its TMEM and exits.
+// A tile is 128 consecutive entries of the voxel order produced by the map build, so its rows
+// share most of their offset masks; the OR of the 128 masks selects the offsets the tile needs.
+// The work of a CTA is a stream of steps, one per (tile, active offset v, K chunk of <= 64
+// channels). One CTA = 10 warps with fixed roles, synchronised only through mbarriers:
+//   warp 0    scheduler: per tile, loads its rows (order) and mask words, ORs them, and splits
+//             the active offsets into contexts of <= 16; for each context it loads the 16 x 128
+//             neighbour indices (only where a row's mask bit is set; -1 elsewhere) into one of
+//             three context buffers by cp.async and hands the buffer over;
+//   warps 1-4 gatherers: warp g owns tile rows 32g..32g+31 and runs its own cp.async pipeline:
+//             per step, groups of KC/8 lanes copy whole feature rows (16 B per lane, zero-fill
+//             for a missing neighbour) into the A stage, straight into the 32/64/128-byte
+//             swizzled K-major layout; a step is signalled on the stage's "full" mbarrier once
+//             its copies have landed (cp.async.wait_group, proxy fence, arrive), D-1 steps
+//             behind the issue, so several steps per warp are in flight; warp 1 lane 0 also
+//             loads W[:, v, kc] into the B stage by TMA (bytes counted on the same mbarrier);
+//   warp 5    MMA: one thread waits for a full stage, issues KC/16 tcgen05.mma
+//             (M=128, N=Co, K=16) into the tile's TMEM accumulator, and commits to the stage's
+//             "empty" mbarrier (and, after a tile's last step, to the accumulator's);
+//   warps 6-9 epilogue: TMEM lanes 32*(w%4).. -> registers, + bias, one rounding, one 16-byte
+//             store per 8 outputs; two accumulators alternate so the next tile's MMAs run while
+//             a tile is written out.
+// Gatherers never wait on the scheduler while holding landed-but-unsignalled steps (they
+// flush first), so no wait depends on itself. Every wait is bounded (2 s); a timeout sets an
+// abort flag that ends every role, raises SPCONV_STATUS_WAIT_TIMEOUT, and the CTA waits
+// (bounded) for its copies and MMAs before it frees TMEM and exits.
+#include <cuda.h>
+#include <mutex>
+
 #include "common.cuh"
 #include "conv_internal.h"
 
 namespace spconv {
 
-constexpr int kTcThreads = 128;
+constexpr int kTcWarps = 10;
+constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTileM = 128;
-constexpr int kMaskPrefetchWords = 4;      // next-tile mask words held in registers (V <= 128)
+constexpr int kChunk = 16;          // active offsets per context
+constexpr int kCtxBufs = 3;
+constexpr int kTileRing = 4;        // tiles whose rows the epilogue may still need
+constexpr int kMaxMaskWords = 4;    // offset masks are used for V <= 128 (else all offsets run)
+constexpr int kMaxStages = 8;
+constexpr int kGatherWarps = 4;
+constexpr int kWarpSched = 0, kWarpGather = 1, kWarpMma = 5, kWarpEpi = 6;
+constexpr uint32_t kInfoFirst = 1u << 30, kInfoLast = 1u << 31, kInfoEnd = 0x3fffffffu;
+constexpr int kCtxFirst = 1, kCtxLast = 2, kCtxEnd = 8;
 
 template <int CI, int CO>
 struct TcCfg {
-    static constexpr int kABytes = kTileM * CI * 2;
-    static constexpr int kBBytes = CO * CI * 2;
-    // Gathers run kAhead = kStages - 2 offsets ahead of the MMA: a refilled stage was last
-    // read by the MMA two offsets back, so its completion is off the critical path.
-    // Small stages: five (three ahead); mid-size: four; Ci = Co = 128: three (one ahead).
+    static constexpr int KC = CI > 64 ? 64 : CI;          // channels per K step
+    static constexpr int NKC = CI / KC;
+    static constexpr int kRowBytes = KC * 2;               // = swizzle width (32, 64, 128)
+    static constexpr int kLanesPerRow = kRowBytes / 16;    // = rows per lane in a gather warp
+    static constexpr int kABytes = kTileM * kRowBytes;
+    static constexpr int kBBytes = CO * kRowBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = kStageBytes <= 8 * 1024 ? 6 : (kStageBytes <= 16 * 1024 ? 5 : (kStageBytes <= 32 * 1024 ? 4 : 3));
-    static constexpr int kAhead = kStages - 2;
-    static constexpr int kTmemCols = CO < 32 ? 32 : CO;
-    static constexpr int kAuxBytes = 256;
-    static constexpr int kSmemBytes = kStages * (kABytes + kBBytes) + kAuxBytes + 128;
+    static constexpr int kNBytes = kCtxBufs * kChunk * kTileM * 4;
+    static constexpr int kFixedBytes = kNBytes + kCtxBufs * kChunk * 4 + kCtxBufs * 16 +
+                                       kTileRing * kTileM * 4 + kMaxStages * 4 + 40 * 8 + 16;
+    // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
+    static constexpr int kBudget = kStageBytes <= 12 * 1024 ? 110 * 1024 : 219 * 1024;
+    static constexpr int kStagesFit = (kBudget - kFixedBytes - 1024) / kStageBytes;
+    static constexpr int kStages = kStagesFit > kMaxStages ? kMaxStages : (kStagesFit < 3 ? 3 : kStagesFit);
+    static constexpr int kDepth = kStages - 1;             // cp.async groups in flight per gatherer
+    // shared memory layout (offsets from a 1024-byte aligned base)
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kABytes;
+    static constexpr int kOffN = kOffB + kStages * kBBytes;
+    static constexpr int kOffAct = kOffN + kNBytes;
+    static constexpr int kOffCInfo = kOffAct + kCtxBufs * kChunk * 4;
+    static constexpr int kOffTRow = kOffCInfo + kCtxBufs * 16;
+    static constexpr int kOffInfo = kOffTRow + kTileRing * kTileM * 4;
+    static constexpr int kOffBar = kOffInfo + kMaxStages * 4;
+    static constexpr int kOffMisc = kOffBar + 40 * 8;
+    static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
+    static constexpr int kTmemCols = 2 * CO < 32 ? 32 : 2 * CO;   // two accumulators
     static constexpr int kMaxCtasByTmem = 512 / kTmemCols;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kABytes % 1024 == 0 && kBBytes % (8 * kRowBytes) == 0, "swizzle atom alignment");
+    static_assert(kDepth >= 2 && kDepth < kStages, "gather pipeline depth");
 };
 
 template <int N>
 __device__ __forceinline__ void cp_async_wait_upto(int pending) {
-    // wait until at most `pending` (<= N) groups are outstanding
+    // wait until at most `pending` groups are outstanding (at most N: waiting for more is safe)
     if (pending >= N) { cp_async_wait<N>(); return; }
     if constexpr (N > 0) cp_async_wait_upto<N - 1>(pending);
 }
@@ -63,206 +106,438 @@ __device__ __forceinline__ uint32_t full_mask_word(int w, int V) {
     return (V - lo >= 32) ? 0xffffffffu : ((1u << (V - lo)) - 1u);
 }
 
+__device__ __forceinline__ uint32_t sel4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int w) {
+    return w == 0 ? a : (w == 1 ? b : (w == 2 ? c : d));
+}
+
 template <int CI, int CO, typename T>
-__global__ void __launch_bounds__(kTcThreads)
-conv_tc_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
+__global__ void __launch_bounds__(kTcThreads, 1)
+conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__ feats,
                const T *__restrict__ bias, const int32_t *__restrict__ nbr,
                const uint32_t *__restrict__ masks, const int32_t *__restrict__ order,
-               T *__restrict__ out, int64_t M, int V, int MW, int num_tiles, int32_t *status) {
+               T *__restrict__ out, int64_t M, int V, int MW, int MWS, int num_tiles,
+               int32_t *status) {
     using Cfg = TcCfg<CI, CO>;
+    constexpr int S = Cfg::kStages, KC = Cfg::KC, NKC = Cfg::NKC, RB = Cfg::kRowBytes;
+    constexpr int LPR = Cfg::kLanesPerRow, D = Cfg::kDepth;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-    uint8_t *sA = base;
-    uint8_t *sB = base + Cfg::kStages * Cfg::kABytes;
-    uint8_t *aux = sB + Cfg::kStages * Cfg::kBBytes;
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(aux);               // [Cfg::kStages]
-    uint32_t *s_tmem = reinterpret_cast<uint32_t *>(aux + 64);
-    uint32_t *s_maskw = reinterpret_cast<uint32_t *>(aux + 128);      // [<= 32]
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t sA = smem_u32(base + Cfg::kOffA), sB = smem_u32(base + Cfg::kOffB);
+    int32_t *s_n = reinterpret_cast<int32_t *>(base + Cfg::kOffN);        // [ctx][i][row]
+    int32_t *s_act = reinterpret_cast<int32_t *>(base + Cfg::kOffAct);    // [ctx][i] -> v
+    int4 *s_cinfo = reinterpret_cast<int4 *>(base + Cfg::kOffCInfo);      // [ctx] {k, cnt, flags}
+    int32_t *s_trow = reinterpret_cast<int32_t *>(base + Cfg::kOffTRow);  // [tile % ring][row]
+    uint32_t *s_info = reinterpret_cast<uint32_t *>(base + Cfg::kOffInfo);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(base + Cfg::kOffBar);
+    uint64_t *full = bar, *empty = bar + 8, *cfull = bar + 16, *cempty = bar + 19;
+    uint64_t *afull = bar + 22, *aempty = bar + 24, *tfull = bar + 26, *tempty = bar + 30;
+    uint32_t *s_tmem = reinterpret_cast<uint32_t *>(base + Cfg::kOffMisc);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(base + Cfg::kOffMisc + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < Cfg::kStages; ++s) mbar_init(smem_u32(&mbar[s]), 1);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), kGatherWarps + 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int c = 0; c < kCtxBufs; ++c) {
+            mbar_init(smem_u32(&cfull[c]), 1);
+            mbar_init(smem_u32(&cempty[c]), kGatherWarps);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&afull[b]), 1);
+            mbar_init(smem_u32(&aempty[b]), 4);
+        }
+        for (int t = 0; t < kTileRing; ++t) {
+            mbar_init(smem_u32(&tfull[t]), 1);
+            mbar_init(smem_u32(&tempty[t]), 4);
+        }
+        *s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (warp == 0) {
+    if (warp == kWarpMma) {
         tmem_alloc(smem_u32(s_tmem), Cfg::kTmemCols);
         tmem_relinquish();
     }
+    if (warp == kWarpGather && lane == 0) tma_prefetch_desc(&tmap_w);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    const uint32_t idesc = instr_desc_f16(dtype_traits<T>::mma_format, kTileM, CO);
-    const uint32_t a_stage0 = smem_u32(sA), b_stage0 = smem_u32(sB);
 
-    uint32_t it = 0;          // stage uses issued by this CTA so far
-    bool ok = true;
     // Tiles are taken from the end of the voxel order first: voxels with the most neighbours
-    // sort last, and their tiles (the most active offsets) then start earliest.
+    // sort last, so the tiles with the most active offsets start earliest.
     const int G = gridDim.x;
-    const int my_tiles = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
-    auto row_of = [&](int k) -> int32_t {
-        const int tile = num_tiles - 1 - ((int)blockIdx.x + k * G);
-        const int64_t r = (int64_t)tile * kTileM + tid;
-        int32_t rr = -1;
-        if (r < M) rr = order ? __ldg(order + r) : (int32_t)r;
-        return rr >= M ? -1 : rr;                 // an order entry outside the table is ignored
+    const int nt = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    const bool use_masks = MWS > 0;
+    auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
+        return mbar_wait_or_abort(smem_u32(b), parity, s_abort);
     };
-    auto mask_word = [&](int32_t rr, int w) -> uint32_t {
-        if (rr < 0) return 0u;
-        return masks ? __ldg(masks + (int64_t)rr * MW + w) : full_mask_word(w, V);
-    };
-    // Row and mask words of the next tile are loaded while the current tile runs.
-    int32_t row_next = my_tiles > 0 ? row_of(0) : -1;
-    uint32_t mk_next[kMaskPrefetchWords];
-#pragma unroll
-    for (int w = 0; w < kMaskPrefetchWords; ++w) mk_next[w] = w < MW ? mask_word(row_next, w) : 0u;
 
-    for (int k = 0; k < my_tiles; ++k) {
-        const int32_t row = row_next;
-        uint32_t mk[kMaskPrefetchWords];
+    if (warp == kWarpSched) {
+        // ------------------------------------------------------------------ scheduler
+        // Lane l handles rows 4l..4l+3 of each tile. Rows are loaded three tiles ahead and
+        // mask words two tiles ahead, so their latency hides behind the tiles in between.
+        auto load_rows = [&](int k, int32_t (&r)[4]) {
 #pragma unroll
-        for (int w = 0; w < kMaskPrefetchWords; ++w) mk[w] = mk_next[w];
-        if (k + 1 < my_tiles) row_next = row_of(k + 1);
-
-        __syncthreads();                          // previous tile done with s_maskw and TMEM
-        if (tid < MW) s_maskw[tid] = 0u;
-        __syncthreads();
-        for (int w = 0; w < MW; ++w) {
-            uint32_t m = 0;
-            if (MW <= kMaskPrefetchWords) {
-#pragma unroll
-                for (int q = 0; q < kMaskPrefetchWords; ++q) if (q == w) m = mk[q];
-            } else {
-                m = mask_word(row, w);
+            for (int j = 0; j < 4; ++j) {
+                r[j] = -1;
+                if (k < nt) {
+                    const int64_t p = (int64_t)(num_tiles - 1 - ((int)blockIdx.x + k * G)) * kTileM + 4 * lane + j;
+                    if (p < M) r[j] = order ? __ldg(order + p) : (int32_t)p;
+                }
             }
-            m = __reduce_or_sync(0xffffffffu, m) & full_mask_word(w, V);
-            if (lane == 0 && m) atomicOr(&s_maskw[w], m);
-        }
-        __syncthreads();
-
-        // Active offsets are consumed in ascending v. Gathers run kAhead offsets ahead of the
-        // MMA, so several are in flight per thread while the tensor core works.
-        const int32_t *nrow = nbr + (int64_t)(row < 0 ? 0 : row) * V;
-        int nact = 0;
-        for (int w = 0; w < MW; ++w) nact += __popc(s_maskw[w]);
-        int iw = 0;                                 // issue-side cursor over the mask words
-        uint32_t im = s_maskw[0];
-        const uint32_t it0 = it;
-        auto issue = [&](int jj) {
-            while (im == 0u && ++iw < MW) im = s_maskw[iw];
-            const int v = iw * 32 + __ffs(im) - 1;
-            im &= im - 1u;
-            const uint32_t slot = it0 + (uint32_t)jj;
-            const int s = (int)(slot % Cfg::kStages);
-            const uint32_t use = slot / Cfg::kStages;
-            if (use > 0 && !mbar_wait_bounded(smem_u32(&mbar[s]), (use - 1u) & 1u)) ok = false;
-            int32_t n = row >= 0 ? __ldg(nrow + v) : -1;
-            if (n >= M) n = -1;                   // rows outside the feature table read as missing
-            const T *src = feats + (int64_t)(n < 0 ? 0 : n) * CI;
-            const uint32_t a_st = a_stage0 + s * Cfg::kABytes;
-            const uint32_t b_st = b_stage0 + s * Cfg::kBBytes;
-#pragma unroll
-            for (int c = 0; c < CI / 8; ++c)
-                cp_async_16(a_st + (uint32_t)(c * kTileM + tid) * 16u, src + c * 8, n < 0 ? 0u : 16u);
-#pragma unroll
-            for (int q = tid; q < CO * (CI / 8); q += kTcThreads) {
-                const int co = q % CO, c = q / CO;
-                cp_async_16(b_st + (uint32_t)(c * CO + co) * 16u,
-                            weight + ((int64_t)co * V + v) * CI + c * 8, 16u);
-            }
-            cp_async_commit();
         };
-        int issued = 0;
-        while (issued < nact && issued < Cfg::kAhead) issue(issued++);
-        int j = 0;
-        for (; j < nact; ++j) {
-            if (issued < nact) issue(issued++);
-            cp_async_wait_upto<Cfg::kAhead>(issued - j - 1);   // offset j's group has landed
+        auto load_masks = [&](int32_t (&r)[4], uint32_t (&m)[4][kMaxMaskWords]) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if ((uint32_t)r[j] >= (uint32_t)M) r[j] = -1;   // order entries outside the table are ignored
+#pragma unroll
+                for (int w = 0; w < kMaxMaskWords; ++w)
+                    m[j][w] = (w < MWS && r[j] >= 0) ? __ldg(masks + (int64_t)r[j] * MW + w) : 0u;
+            }
+        };
+        int32_t rA[4], rB[4], rC[4];
+        uint32_t mA[4][kMaxMaskWords], mB[4][kMaxMaskWords];
+        load_rows(0, rA);
+        load_rows(1, rB);
+        load_rows(2, rC);
+        load_masks(rA, mA);
+        load_masks(rB, mB);
+        int g = 0;                           // contexts handed out
+        int pend = -1;                       // context buffer whose index loads are in flight
+        bool ok = true;
+        auto publish_pending = [&](bool all) {
+            if (pend < 0) return;
+            if (all) cp_async_wait<0>();
+            else cp_async_wait<1>();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&cfull[pend]));
+            pend = -1;
+        };
+        for (int k = 0; k < nt && ok; ++k) {
+            uint32_t tm[kMaxMaskWords];
+            int nact = 0;
+#pragma unroll
+            for (int w = 0; w < kMaxMaskWords; ++w) {
+                uint32_t m = 0u;
+                if (w < MWS) {
+                    m = __reduce_or_sync(0xffffffffu, mA[0][w] | mA[1][w] | mA[2][w] | mA[3][w]) &
+                        full_mask_word(w, V);
+                }
+                tm[w] = m;
+                nact += __popc(m);
+            }
+            if (!use_masks) nact = V;
+            const bool fake = nact == 0;     // no offset: one step of zeros gives the bias rows
+            int left = fake ? 1 : nact;
+
+            const int t = k % kTileRing;
+            if (k >= kTileRing && !wait(&tempty[t], (uint32_t)(((k / kTileRing) - 1) & 1))) { ok = false; break; }
+            *reinterpret_cast<int4 *>(&s_trow[t * kTileM + 4 * lane]) = make_int4(rA[0], rA[1], rA[2], rA[3]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tfull[t]));
+
+            int w = 0, vnext = 0;
+            uint32_t bits = tm[0];
+            bool first = true;
+            while (left > 0) {
+                const int cnt = left < kChunk ? left : kChunk;
+                const int cb = g % kCtxBufs;
+                if (g >= kCtxBufs && !wait(&cempty[cb], (uint32_t)(((g / kCtxBufs) - 1) & 1))) { ok = false; break; }
+                int32_t *dn = &s_n[cb * kChunk * kTileM + 4 * lane];
+                for (int i = 0; i < cnt; ++i) {
+                    int v = 0;
+                    if (!fake) {
+                        if (!use_masks) {
+                            v = vnext++;
+                        } else {
+                            while (bits == 0u && w + 1 < MWS) {
+                                ++w;
+                                bits = sel4(tm[0], tm[1], tm[2], tm[3], w);
+                            }
+                            v = bits ? w * 32 + __ffs(bits) - 1 : 0;
+                            bits &= bits - 1u;
+                        }
+                    }
+                    if (lane == 0) s_act[cb * kChunk + i] = v;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        bool have = rA[j] >= 0 && !fake;
+                        if (have && use_masks)
+                            have = ((sel4(mA[j][0], mA[j][1], mA[j][2], mA[j][3], v >> 5) >> (v & 31)) & 1u) != 0u;
+                        int32_t *d = dn + i * kTileM + j;
+                        if (have) cp_async_4(smem_u32(d), nbr + (int64_t)rA[j] * V + v);
+                        else *d = -1;
+                    }
+                }
+                cp_async_commit();
+                left -= cnt;
+                if (lane == 0) s_cinfo[cb] = make_int4(k, cnt, (first ? kCtxFirst : 0) | (left == 0 ? kCtxLast : 0), 0);
+                first = false;
+                publish_pending(false);      // the previous context's loads have landed
+                pend = cb;
+                ++g;
+            }
+            if (!ok) break;
+            // next tile: rows of k+3 and masks of k+2 start loading now
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                rA[j] = rB[j];
+                rB[j] = rC[j];
+#pragma unroll
+                for (int q = 0; q < kMaxMaskWords; ++q) mA[j][q] = mB[j][q];
+            }
+            load_masks(rB, mB);
+            load_rows(k + 3, rC);
+        }
+        publish_pending(true);
+        if (ok) {                            // end marker
+            const int cb = g % kCtxBufs;
+            if (g < kCtxBufs || wait(&cempty[cb], (uint32_t)(((g / kCtxBufs) - 1) & 1))) {
+                if (lane == 0) s_cinfo[cb] = make_int4(0, 0, kCtxEnd, 0);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&cfull[cb]));
+            }
+        }
+        cp_async_wait_all();
+    } else if (warp >= kWarpGather && warp < kWarpGather + kGatherWarps) {
+        // ------------------------------------------------------------------ gatherers
+        // Lane L copies chunk L % LPR of tile rows 32g + (L / LPR) * LPR + q, q < LPR: each
+        // warp instruction moves 32 / LPR whole rows, and a lane's LPR neighbour indices are
+        // consecutive in the context buffer.
+        const int gw = warp - kWarpGather;
+        const bool b_loader = gw == 0 && lane == 0;
+        const int chunk = lane % LPR;
+        const int row0 = 32 * gw + (lane / LPR) * LPR;       // first of this lane's rows
+        uint32_t dst[LPR];
+#pragma unroll
+        for (int q = 0; q < LPR; ++q) {
+            const int r = row0 + q;
+            dst[q] = (uint32_t)(r * RB + ((chunk ^ ((r * RB >> 7) & (LPR - 1))) << 4));
+        }
+        int g = 0, step = 0, sig = 0;       // contexts consumed, steps issued, steps signalled
+        bool ok = true;
+        auto signal_one = [&]() {            // the oldest unsignalled step has landed
             fence_proxy_async_smem();
-            if (!__syncthreads_and(ok)) { ok = false; break; }
-            const int s = (int)((it0 + (uint32_t)j) % Cfg::kStages);
-            if (tid == 0) {
-                tc_fence_after();
-                const uint32_t a_st = a_stage0 + s * Cfg::kABytes;
-                const uint32_t b_st = b_stage0 + s * Cfg::kBBytes;
-#pragma unroll
-                for (int kk = 0; kk < CI / 16; ++kk) {
-                    const uint64_t ad = smem_desc_kmajor_noswizzle(a_st + kk * 2 * (kTileM * 16), kTileM * 16, 128);
-                    const uint64_t bd = smem_desc_kmajor_noswizzle(b_st + kk * 2 * (CO * 16), CO * 16, 128);
-                    tc_mma_f16(tmem, ad, bd, idesc, (j | kk) != 0 ? 1u : 0u);
-                }
-                tc_commit(smem_u32(&mbar[s]));
-            }
-        }
-        it = it0 + (uint32_t)j;
-        if (!ok) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&full[sig % S]));
+            ++sig;
+        };
+        auto flush = [&]() {
             cp_async_wait<0>();
-            break;
-        }
-        // The next tile's mask words (its row load has landed by now).
-#pragma unroll
-        for (int w = 0; w < kMaskPrefetchWords; ++w)
-            mk_next[w] = (k + 1 < my_tiles && w < MW && MW <= kMaskPrefetchWords) ? mask_word(row_next, w) : 0u;
-        if (j > 0) {
-            const uint32_t last = it - 1u;
-            if (!mbar_wait_bounded(smem_u32(&mbar[last % Cfg::kStages]), (last / Cfg::kStages) & 1u)) ok = false;
-        }
-        if (!__syncthreads_and(ok)) { ok = false; break; }
-        tc_fence_after();
-
-        // Epilogue: TMEM lanes 32*warp .. 32*warp+31 hold this warp's 32 rows.
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-        T *orow = out + (int64_t)(row < 0 ? 0 : row) * CO;
-#pragma unroll
-        for (int cc = 0; cc < CO / 16; ++cc) {
-            uint32_t acc[16];
-            if (j > 0) {
-                tmem_ld16(taddr + cc * 16, acc);
-                tc_wait_ld();
-            } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) acc[e] = 0u;
-            }
-            if (row >= 0) {
-                float f[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    f[e] = __uint_as_float(acc[e]);
-                    if (bias) f[e] += dtype_traits<T>::to_f(bias[cc * 16 + e]);
+            while (sig < step) signal_one();
+        };
+        for (;;) {
+            const int cb = g % kCtxBufs;
+            const uint32_t cpar = (uint32_t)((g / kCtxBufs) & 1);
+            if (!mbar_test(smem_u32(&cfull[cb]), cpar)) flush();   // never wait on the scheduler with steps unsignalled
+            if (!wait(&cfull[cb], cpar)) { ok = false; break; }
+            const int4 ci = s_cinfo[cb];
+            if (ci.z & kCtxEnd) break;
+            const int k = ci.x, cnt = ci.y;
+            const bool cfirst = (ci.z & kCtxFirst) != 0, clast = (ci.z & kCtxLast) != 0;
+            for (int i = 0; i < cnt && ok; ++i) {
+                const int v = s_act[cb * kChunk + i];
+                int32_t n[LPR];
+                const int32_t *np = &s_n[(cb * kChunk + i) * kTileM + row0];
+                if constexpr (LPR == 8) {
+                    const int4 a = reinterpret_cast<const int4 *>(np)[0], b = reinterpret_cast<const int4 *>(np)[1];
+                    n[0] = a.x; n[1] = a.y; n[2] = a.z; n[3] = a.w; n[4] = b.x; n[5] = b.y; n[6] = b.z; n[7] = b.w;
+                } else if constexpr (LPR == 4) {
+                    const int4 a = reinterpret_cast<const int4 *>(np)[0];
+                    n[0] = a.x; n[1] = a.y; n[2] = a.z; n[3] = a.w;
+                } else {
+                    const int2 a = reinterpret_cast<const int2 *>(np)[0];
+                    n[0] = a.x; n[1] = a.y;
                 }
-                uint4 p0, p1;
-                p0.x = pack2<T>(f[0], f[1]);   p0.y = pack2<T>(f[2], f[3]);
-                p0.z = pack2<T>(f[4], f[5]);   p0.w = pack2<T>(f[6], f[7]);
-                p1.x = pack2<T>(f[8], f[9]);   p1.y = pack2<T>(f[10], f[11]);
-                p1.z = pack2<T>(f[12], f[13]); p1.w = pack2<T>(f[14], f[15]);
-                uint4 *dst = reinterpret_cast<uint4 *>(orow + cc * 16);
-                dst[0] = p0;
-                dst[1] = p1;
+#pragma unroll
+                for (int kc = 0; kc < NKC; ++kc) {
+                    const int s = step % S, u = step / S;
+                    if (u > 0 && !wait(&empty[s], (uint32_t)((u - 1) & 1))) { ok = false; break; }
+                    if (b_loader) {
+                        s_info[s] = (uint32_t)k | ((cfirst && i == 0 && kc == 0) ? kInfoFirst : 0u) |
+                                    ((clast && i == cnt - 1 && kc == NKC - 1) ? kInfoLast : 0u);
+                        mbar_arrive_expect_tx(smem_u32(&full[s]), (uint32_t)Cfg::kBBytes);
+                        tma_load_2d(sB + s * Cfg::kBBytes, &tmap_w, v * CI + kc * KC, 0, smem_u32(&full[s]));
+                    }
+                    const uint32_t a_st = sA + s * Cfg::kABytes;
+                    const T *src = feats + kc * KC + chunk * 8;
+#pragma unroll
+                    for (int q = 0; q < LPR; ++q) {
+                        // rows outside the feature table (and missing neighbours) read as zeros
+                        const bool have = (uint32_t)n[q] < (uint32_t)M;
+                        cp_async_16(a_st + dst[q], src + (int64_t)(have ? n[q] : 0) * CI, have ? 16u : 0u);
+                    }
+                    cp_async_commit();
+                    ++step;
+                    if (step - sig > D - 1) {   // keep D-1 steps in flight; the oldest has landed
+                        cp_async_wait<D - 1>();
+                        signal_one();
+                    }
+                }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&cempty[cb]));
+            ++g;
+        }
+        if (ok) {
+            flush();
+            // end marker: one more "step" carrying no data
+            const int s = step % S, u = step / S;
+            if (u == 0 || wait(&empty[s], (uint32_t)((u - 1) & 1))) {
+                if (b_loader) {
+                    s_info[s] = kInfoEnd;
+                    mbar_arrive(smem_u32(&full[s]));
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&full[s]));
             }
         }
-        tc_fence_before();
+        cp_async_wait_all();
+        if (!ok && b_loader) {
+            // wait (bounded) for the weight loads of the last step issued on each stage
+            for (int q = 1; q <= S && q <= step; ++q) {
+                const int st = step - q;
+                mbar_wait_bounded(smem_u32(&full[st % S]), (uint32_t)((st / S) & 1));
+            }
+        }
+    } else if (warp == kWarpMma) {
+        // ------------------------------------------------------------------ MMA
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc_f16(dtype_traits<T>::mma_format, kTileM, CO);
+            int step = 0;
+            for (;;) {
+                const int s = step % S, u = step / S;
+                if (!wait(&full[s], (uint32_t)(u & 1))) break;
+                const uint32_t info = s_info[s];
+                if (info == kInfoEnd) break;
+                const int k = (int)(info & 0x3fffffffu);
+                const bool first = (info & kInfoFirst) != 0u, last = (info & kInfoLast) != 0u;
+                const int b = k & 1, ua = k >> 1;
+                if (first && ua > 0 && !wait(&aempty[b], (uint32_t)((ua - 1) & 1))) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(b * CO);
+#pragma unroll
+                for (int kk = 0; kk < KC / 16; ++kk) {
+                    const uint64_t ad = smem_desc_kmajor_swizzled(sA + s * Cfg::kABytes + kk * 32, RB);
+                    const uint64_t bd = smem_desc_kmajor_swizzled(sB + s * Cfg::kBBytes + kk * 32, RB);
+                    tc_mma_f16(d, ad, bd, idesc, (!first || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(smem_u32(&empty[s]));
+                if (last) tc_commit(smem_u32(&afull[b]));
+                ++step;
+            }
+            if (*s_abort && step > 0) {      // wait (bounded) for the MMAs issued so far
+                const int st = step - 1;
+                mbar_wait_bounded(smem_u32(&empty[st % S]), (uint32_t)((st / S) & 1));
+            }
+        }
+    } else if (warp >= kWarpEpi) {
+        // ------------------------------------------------------------------ epilogue
+        constexpr int kCols = CO < 32 ? CO : 32;      // columns per TMEM load batch
+        const int quad = warp & 3;
+        for (int k = 0; k < nt; ++k) {
+            const int b = k & 1, t = k % kTileRing;
+            if (!wait(&afull[b], (uint32_t)((k >> 1) & 1))) break;
+            if (!wait(&tfull[t], (uint32_t)((k / kTileRing) & 1))) break;
+            tc_fence_after();
+            const int32_t row = s_trow[t * kTileM + quad * 32 + lane];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty[t]));
+            const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * CO);
+            T *orow = out + (int64_t)(row < 0 ? 0 : row) * CO;
+#pragma unroll
+            for (int c0 = 0; c0 < CO; c0 += kCols) {
+                uint32_t acc[kCols];
+#pragma unroll
+                for (int m = 0; m < kCols / 8; ++m) tmem_ld8(taddr + c0 + m * 8, &acc[m * 8]);
+                tc_wait_ld();
+                if (row >= 0) {
+#pragma unroll
+                    for (int m = 0; m < kCols / 8; ++m) {
+                        float f[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            f[q] = __uint_as_float(acc[m * 8 + q]);
+                            if (bias) f[q] += dtype_traits<T>::to_f(bias[c0 + m * 8 + q]);
+                        }
+                        uint4 p;
+                        p.x = pack2<T>(f[0], f[1]);
+                        p.y = pack2<T>(f[2], f[3]);
+                        p.z = pack2<T>(f[4], f[5]);
+                        p.w = pack2<T>(f[6], f[7]);
+                        *reinterpret_cast<uint4 *>(orow + c0 + m * 8) = p;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&aempty[b]));
+        }
     }
 
-    if (!ok) {
-        if (tid == 0) {
-            raise_status(status, SPCONV_STATUS_WAIT_TIMEOUT);
-            if (it > 0) {
-                const uint32_t last = it - 1u;
-                mbar_wait_bounded(smem_u32(&mbar[last % Cfg::kStages]), (last / Cfg::kStages) & 1u);
-            }
-        }
-    }
+    __syncwarp();
+    if (*s_abort && tid == 0) raise_status(status, SPCONV_STATUS_WAIT_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, Cfg::kTmemCols);
+    if (warp == kWarpMma) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side: weight tensor map and launch.
+// ---------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn tensor_map_encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D row-major tensor of 16-bit elements: `cols` x `rows`, rows `row_stride` bytes apart;
+// box = box_cols x box_rows; swizzle width = box_cols * 2 bytes.
+static bool make_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t cols, uint64_t rows,
+                         uint64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (!enc) {
+        set_error("tcgen05 conv: cuTensorMapEncodeTiled is not available from the driver");
+        return false;
+    }
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {row_stride};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const uint32_t wbytes = box_cols * 2;
+    const CUtensorMapSwizzle sw = wbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : (wbytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(ptr), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("tcgen05 conv: tensor map encoding failed (CUresult %d)", (int)r);
+        return false;
+    }
+    return true;
 }
 
 template <int CI, int CO, typename T>
 static int launch_tc(const ConvArgs &a) {
     using Cfg = TcCfg<CI, CO>;
     auto kern = conv_tc_kernel<CI, CO, T>;
+    const int MWS = (a.masks && a.MW <= kMaxMaskWords) ? a.MW : 0;
     // Shared memory is padded so that no more CTAs fit on an SM than its 512 TMEM columns
     // serve (228 KB of shared memory per SM, 1 KB reserved per CTA): tcgen05.alloc never waits.
     constexpr int kSmemForTmem = (228 * 1024) / (Cfg::kMaxCtasByTmem + 1);
@@ -275,26 +550,25 @@ static int launch_tc(const ConvArgs &a) {
     if (!attr_done[dev]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_launch("conv_tc: set max dynamic shared memory");
-        // Without a carveout preference the occupancy query (and the launch) may assume a
-        // small shared-memory carveout and allow a single CTA per SM.
         if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return check_launch("conv_tc: set shared memory carveout");
         int occ = occupancy_per_sm((const void *)kern, kTcThreads, smem);
         if (occ > Cfg::kMaxCtasByTmem) occ = Cfg::kMaxCtasByTmem;
-        occ_cache[dev] = occ;
+        occ_cache[dev] = occ < 1 ? 1 : occ;
         attr_done[dev] = true;
     }
+    CUtensorMap tw;
+    if (!make_tmap_2d(&tw, a.weight, (uint64_t)a.V * CI, (uint64_t)CO, (uint64_t)a.V * CI * 2, Cfg::KC, CO))
+        return SPCONV_ERR_CUDA;
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int occ = occ_cache[dev];
     const int num_tiles = (int)((a.M + kTileM - 1) / kTileM);
-    int grid = sms * occ;
+    int grid = sms * occ_cache[dev];
     if (grid > num_tiles) grid = num_tiles;
     if (grid < 1) grid = 1;
-    kern<<<grid, kTcThreads, smem, a.stream>>>(
-        (const T *)a.feats, (const T *)a.weight, (const T *)a.bias, a.nbr, a.masks, a.order,
-        (T *)a.out, a.M, a.V, a.MW, num_tiles, a.status);
+    kern<<<grid, kTcThreads, smem, a.stream>>>(tw, (const T *)a.feats, (const T *)a.bias, a.nbr, a.masks,
+                                               a.order, (T *)a.out, a.M, a.V, a.MW, MWS, num_tiles, a.status);
     return check_launch("conv_tc_kernel");
 }
 
