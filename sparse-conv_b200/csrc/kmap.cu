@@ -695,6 +695,191 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
 }
 
 // ---------------------------------------------------------------------------------------
+// 2d. Map build for other kernels with V <= 128 offsets whose z extent spans <= 32 cells
+//     (e.g. 5x5x5), with the occupancy bitmap: the same two phases as 2c with the kernel
+//     shape at run time. Phase 1 reads one funnel-shifted bitmap window per (dx, dy) column
+//     (four columns' loads in flight) and keeps the in-range z cells of it; phase 2 probes
+//     the candidates, four at a time. Rows are staged in shared memory pre-filled with -1.
+// ---------------------------------------------------------------------------------------
+constexpr int kMapColsThreads = 128;
+constexpr int kMapColsMaxV = 128;
+
+__device__ __forceinline__ void or_word4(uint32_t (&m)[4], int w, uint32_t x) {
+    if (w == 0) m[0] |= x;
+    else if (w == 1) m[1] |= x;
+    else if (w == 2) m[2] |= x;
+    else if (w == 3) m[3] |= x;
+}
+__device__ __forceinline__ void clear_bit4(uint32_t (&m)[4], int v) {
+    const uint32_t x = ~(1u << (v & 31));
+    if ((v >> 5) == 0) m[0] &= x;
+    else if ((v >> 5) == 1) m[1] &= x;
+    else if ((v >> 5) == 2) m[2] &= x;
+    else m[3] &= x;
+}
+// Lowest set bit of a 128-bit mask (cleared), or -1.
+__device__ __forceinline__ int pop_lowest4(uint32_t (&m)[4]) {
+    if (m[0]) { const int b = __ffs(m[0]) - 1; m[0] &= m[0] - 1u; return b; }
+    if (m[1]) { const int b = __ffs(m[1]) - 1; m[1] &= m[1] - 1u; return 32 + b; }
+    if (m[2]) { const int b = __ffs(m[2]) - 1; m[2] &= m[2] - 1u; return 64 + b; }
+    if (m[3]) { const int b = __ffs(m[3]) - 1; m[3] &= m[3] - 1u; return 96 + b; }
+    return -1;
+}
+
+__global__ void __launch_bounds__(kMapColsThreads)
+map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Kw, int Kh, int Kd,
+                int Dw, int Dh, int Dd, int V, int MW, const unsigned long long *__restrict__ table,
+                const uint32_t *__restrict__ bitmap, int64_t bm_words, uint64_t gmask, uint32_t shift,
+                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, uint32_t *cursor,
+                uint32_t *done_counter, int32_t *status) {
+    __shared__ uint32_t s_hist[kOrderBuckets];
+    __shared__ uint32_t s_is_last;
+    __shared__ uint32_t s_warp[kMapColsThreads / 32];
+    extern __shared__ int4 s_stage4[];                           // [kMapColsThreads * V] int32, padded to 16 B
+    int32_t *s_stage = reinterpret_cast<int32_t *>(s_stage4);
+
+    const int tid = threadIdx.x;
+    const int64_t i0 = (int64_t)blockIdx.x * kMapColsThreads;
+    const int nvox = (M - i0) < (int64_t)kMapColsThreads ? (int)(M - i0) : kMapColsThreads;
+    const int stage_words = kMapColsThreads * V;
+    for (int j = tid; j < kOrderBuckets; j += kMapColsThreads) s_hist[j] = 0u;
+    for (int j = tid; j < (stage_words + 3) / 4; j += kMapColsThreads) s_stage4[j] = make_int4(-1, -1, -1, -1);
+
+    const bool valid = tid < nvox;
+    const int64_t i = i0 + tid;
+    int4 c = make_int4(0, 0, 0, 0);
+    if (valid) c = __ldg(coords + i);
+    const int64_t HD = (int64_t)H * D;
+    const int64_t key_c = (((int64_t)c.x * W + c.y) * H + c.z) * D + c.w;
+    const int rw = Kw / 2, rh = Kh / 2, rd = Kd / 2;
+    const int zlo = max(c.w - rd * Dd, 0);                      // window starts at the lowest in-range cell
+    // in-range z cells of a column and their bit positions in the window
+    uint32_t zsel = 0;
+    for (int cz = 0; cz < Kd; ++cz) {
+        const int z = c.w + (cz - rd) * Dd;
+        if (z >= 0 && z < D) zsel |= 1u << cz;
+    }
+    auto extract = [&](uint32_t win) -> uint32_t {              // window bits -> Kd column bits
+        if (Dd == 1) {
+            const int s0 = zlo - (c.w - rd);                    // cells below z = 0 (>= 0)
+            return (s0 < 32 ? (win << s0) : 0u) & zsel;
+        }
+        uint32_t r = 0;
+        for (int cz = 0; cz < Kd; ++cz)
+            if ((zsel >> cz) & 1u) r |= ((win >> (c.w + (cz - rd) * Dd - zlo)) & 1u) << cz;
+        return r;
+    };
+
+    // Phase 1: candidate offsets.
+    uint32_t cand[4] = {0u, 0u, 0u, 0u};
+    const int ncol = Kw * Kh;
+    if (valid) {
+        for (int q0 = 0; q0 < ncol; q0 += 4) {
+            uint32_t lo[4], hi[4];
+            int64_t kb[4];
+            bool in[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u;
+                const int cx = q / Kh, cy = q - (q / Kh) * Kh;
+                const int x = c.y + (cx - rw) * Dw, y = c.z + (cy - rh) * Dh;
+                in[u] = q < ncol && x >= 0 && x < W && y >= 0 && y < H;
+                lo[u] = hi[u] = 0u;
+                kb[u] = 0;
+                if (in[u]) {
+                    kb[u] = key_c + (int64_t)(cx - rw) * Dw * HD + (int64_t)(cy - rh) * Dh * D + (zlo - c.w);
+                    const int64_t wi = kb[u] >> 5;
+                    lo[u] = __ldg(bitmap + wi);
+                    hi[u] = __ldg(bitmap + (wi + 1 < bm_words ? wi + 1 : wi));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (in[u]) {
+                    const uint32_t bits = extract(__funnelshift_r(lo[u], hi[u], (uint32_t)(kb[u] & 31)));
+                    const int v0 = (q0 + u) * Kd, w = v0 >> 5, sft = v0 & 31;
+                    or_word4(cand, w, bits << sft);
+                    if (sft + Kd > 32 && sft > 0) or_word4(cand, w + 1, bits >> (32 - sft));
+                }
+            }
+        }
+    }
+    const int vc = V / 2;                                       // the centre entry is the voxel itself
+    clear_bit4(cand, vc);
+
+    __syncthreads();                                            // hist zeroed, stage pre-filled
+    uint32_t bits[4] = {0u, 0u, 0u, 0u};
+    if (valid) {
+        s_stage[tid * V + vc] = (int32_t)i;
+        or_word4(bits, vc >> 5, 1u << (vc & 31));
+    }
+
+    // Phase 2: probe candidate offsets, kK3Batch in flight.
+    bool wrapped = false;
+    while (cand[0] | cand[1] | cand[2] | cand[3]) {
+        int vv[kK3Batch];
+        uint32_t key[kK3Batch];
+        uint64_t grp[kK3Batch];
+        unsigned long long word[kK3Batch][kGroup];
+#pragma unroll
+        for (int b = 0; b < kK3Batch; ++b) {
+            const int v = pop_lowest4(cand);
+            vv[b] = v;
+            if (v >= 0) {
+                const int cx = v / (Kh * Kd), rem = v - cx * (Kh * Kd);
+                const int cy = rem / Kd, cz = rem - cy * Kd;
+                const int64_t kn = key_c + (int64_t)(cx - rw) * Dw * HD + (int64_t)(cy - rh) * Dh * D + (cz - rd) * Dd;
+                key[b] = (uint32_t)kn;
+                grp[b] = home32(key[b], shift);
+                load_group(table, grp[b], word[b]);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < kK3Batch; ++b) {
+            if (vv[b] >= 0) {
+                int32_t r = table_resolve<false>(table, nullptr, gmask, key[b], grp[b], word[b]);
+                if (r == -2) { wrapped = true; r = -1; }
+                if (r >= 0) {
+                    s_stage[tid * V + vv[b]] = r;
+                    or_word4(bits, vv[b] >> 5, 1u << (vv[b] & 31));
+                }
+            }
+        }
+    }
+    if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
+    {
+        uint32_t pc = 0, h = 0x9e3779b9u;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            if (w < MW) {
+                if (valid) masks[i * (int64_t)MW + w] = bits[w];
+                pc += __popc(bits[w]);
+                h = fmix32(h ^ bits[w]);
+            }
+        }
+        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t active = __ballot_sync(0xffffffffu, valid);
+        if (valid) aggregated_inc(s_hist, k, active);
+    }
+    __syncthreads();
+    {
+        // The block's rows form one contiguous range of the map.
+        int32_t *out = nbr + i0 * (int64_t)V;
+        const int total = nvox * V;
+        if (((uintptr_t)out & 15u) == 0) {
+            const int n4 = total >> 2;
+            int4 *dst = reinterpret_cast<int4 *>(out);
+            for (int e = tid; e < n4; e += kMapColsThreads) dst[e] = s_stage4[e];
+            for (int e = (n4 << 2) + tid; e < total; e += kMapColsThreads) out[e] = s_stage[e];
+        } else {
+            for (int e = tid; e < total; e += kMapColsThreads) out[e] = s_stage[e];
+        }
+    }
+    block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+}
+
+// ---------------------------------------------------------------------------------------
 // 3. Counting-sort scatter of voxel ids by order key.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kOrderThreads)
@@ -819,6 +1004,18 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         k3_fn<<<grid, kMapK3Threads, 0, stream>>>(
             (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, table, bitmap, L.bitmap_words, gmask, shift,
             neighbor_map, masks, hist, cursor, counter, status);
+    } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
+        const size_t smem = ((size_t)kMapColsThreads * V * sizeof(int32_t) + 15) / 16 * 16;
+        static bool cols_attr_done = false;
+        if (!cols_attr_done) {
+            cudaFuncSetAttribute(map_kernel_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+            cols_attr_done = true;
+        }
+        const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
+        stage_mark(SPCONV_STAGE_MAP, 0, stream);
+        map_kernel_cols<<<grid, kMapColsThreads, smem, stream>>>(
+            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, table, bitmap, L.bitmap_words,
+            gmask, shift, neighbor_map, masks, hist, cursor, counter, status);
     } else if (bitmap && Kd <= kColBatchMax) {
         // 256 voxels per block while their staged rows fit in 64 KB, else 128.
         const int nthr = ((size_t)kMapBmMaxThreads * (V | 1) * 4 <= 64 * 1024) ? kMapBmMaxThreads : 128;
