@@ -98,6 +98,19 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
 
 
+def _traffic_per_launch(key: str):
+    """DRAM bytes (read + write) per launch of a kernel, from the committed ncu summary
+    `profiles/traffic_per_launch.txt` (lines `workload:kernel bytes`), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == key:
+            return int(parts[1])
+    return None
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -192,6 +205,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="run this many eager forwards of the workload and exit (a target for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -207,7 +222,7 @@ def main():
                                              device_id=dev)
         pg = torch.distributed.group.WORLD
 
-    from sparseconv import _native, synthetic
+    from sparseconv import _native, shards, synthetic
     from sparseconv.ops.submanifold_conv3d import Algorithm, sparse_submanifold_conv3d
 
     w = synthetic.make(args.workload, seed=rank)
@@ -221,6 +236,14 @@ def main():
 
     def step():
         return sparse_submanifold_conv3d(feats, coords, shape, weight, algorithm=Algorithm.IMPLICIT_GEMM)
+
+    if args.profile_steps > 0:
+        for _ in range(args.profile_steps):
+            step()
+        torch.cuda.synchronize()
+        _native.check_errors(dev)
+        print("profile steps done:", args.workload, w.num_voxels, "voxels x", args.profile_steps)
+        return 0
 
     for _ in range(args.warmup):
         out, cache = step()
@@ -281,14 +304,8 @@ def main():
     torch.cuda.synchronize()
     stage = _native.stage_times_ms()
     _native.stage_timing(0)
-    t = torch.tensor([step_ms], dtype=torch.float64, device=dev)
-    if pg is not None:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    max_ms = float(t.item())
-    total_voxels = torch.tensor([w.num_voxels], dtype=torch.float64, device=dev)
-    if pg is not None:
-        torch.distributed.all_reduce(total_voxels)
-    voxels_all = float(total_voxels.item())
+    max_ms = shards.max_over_ranks(step_ms)          # step time: the slowest rank
+    voxels_all = shards.sum_over_ranks(w.num_voxels)  # whole-job work
     value = voxels_all * K / (max_ms / 1e3)
 
     # eager API steps (same work, host Python between the kernels), for reference
@@ -324,10 +341,8 @@ def main():
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if pg is not None:
-        torch.distributed.all_reduce(e2e_ms, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = voxels_all * KE / (float(e2e_ms.item()) / 1e3)
+    e2e_ms = shards.max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = voxels_all * KE / (e2e_ms / 1e3)
     _native.check_errors(dev)
 
     if rank == 0:
@@ -339,10 +354,7 @@ def main():
         dom = max((k for k in per_stage if k in kern_bytes), key=lambda k: per_stage[k][0])
         dom_ms = per_stage[dom][0] / per_stage[dom][1]
         achieved = kern_bytes[dom] / (dom_ms / 1e3) / 1e9
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tp):
-            traffic = json.load(open(tp)).get(f"{args.workload}:{dom}")
+        traffic = _traffic_per_launch(f"{args.workload}:{dom}")
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": max_ms / K, "higher_is_better": True,

@@ -140,18 +140,8 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t addr, uint32_t by
 }
 
 // ---------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), completion on an mbarrier of this CTA. No multicast.
+// TMA (cp.async.bulk.tensor) into this CTA's shared memory, completion on one of its mbarriers.
 // ---------------------------------------------------------------------------------------
-// Four rows (y0..y3) of a 2-D tensor, columns [x, x + box width), into consecutive box rows at
-// `dst`. Rows outside the tensor (negative or >= its height) are filled with zeros.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const void *tmap, int x, int y0, int y1,
-                                            int y2, int y3, uint32_t mbar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n"
-        :: "r"(dst), "l"(tmap), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(mbar)
-        : "memory");
-}
 // One box of a 2-D tensor at (x, y).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int x, int y, uint32_t mbar) {
     asm volatile(
