@@ -40,6 +40,7 @@ constexpr int kTcWarps = 10;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTileM = 128;
 constexpr int kChunk = 16;          // active offsets per context
+constexpr int kNPitch = kChunk + 1; // words per row in a context buffer (conflict-free both ways)
 constexpr int kCtxBufs = 3;
 constexpr int kTileRing = 4;        // tiles whose rows the epilogue may still need
 constexpr int kMaxMaskWords = 4;    // offset masks are used for V <= 128 (else all offsets run)
@@ -58,8 +59,9 @@ struct TcCfg {
     static constexpr int kABytes = kTileM * kRowBytes;
     static constexpr int kBBytes = CO * kRowBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kNBytes = kCtxBufs * kChunk * kTileM * 4;
-    static constexpr int kFixedBytes = kNBytes + kCtxBufs * kChunk * 4 + kCtxBufs * 16 +
+    static constexpr int kNBytes = kCtxBufs * kTileM * kNPitch * 4;
+    static constexpr int kSchedBytes = kMaxMaskWords * kTileM * 4 + kTileM;   // row masks, active list
+    static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kChunk * 4 + kCtxBufs * 16 +
                                        kTileRing * kTileM * 4 + kMaxStages * 4 + 40 * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
     static constexpr int kBudget = kStageBytes <= 12 * 1024 ? 110 * 1024 : 219 * 1024;
@@ -70,7 +72,9 @@ struct TcCfg {
     static constexpr int kOffA = 0;
     static constexpr int kOffB = kOffA + kStages * kABytes;
     static constexpr int kOffN = kOffB + kStages * kBBytes;
-    static constexpr int kOffAct = kOffN + kNBytes;
+    static constexpr int kOffSrm = kOffN + kNBytes;
+    static constexpr int kOffTact = kOffSrm + kMaxMaskWords * kTileM * 4;
+    static constexpr int kOffAct = kOffTact + kTileM;
     static constexpr int kOffCInfo = kOffAct + kCtxBufs * kChunk * 4;
     static constexpr int kOffTRow = kOffCInfo + kCtxBufs * 16;
     static constexpr int kOffInfo = kOffTRow + kTileRing * kTileM * 4;
@@ -123,7 +127,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t sA = smem_u32(base + Cfg::kOffA), sB = smem_u32(base + Cfg::kOffB);
-    int32_t *s_n = reinterpret_cast<int32_t *>(base + Cfg::kOffN);        // [ctx][i][row]
+    int32_t *s_n = reinterpret_cast<int32_t *>(base + Cfg::kOffN);        // [ctx][row][kNPitch]
+    uint32_t *s_srm = reinterpret_cast<uint32_t *>(base + Cfg::kOffSrm);  // scheduler: [word][row] masks
+    uint8_t *s_tact = base + Cfg::kOffTact;                               // scheduler: tile's active offsets
     int32_t *s_act = reinterpret_cast<int32_t *>(base + Cfg::kOffAct);    // [ctx][i] -> v
     int4 *s_cinfo = reinterpret_cast<int4 *>(base + Cfg::kOffCInfo);      // [ctx] {k, cnt, flags}
     int32_t *s_trow = reinterpret_cast<int32_t *>(base + Cfg::kOffTRow);  // [tile % ring][row]
@@ -235,43 +241,59 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             const int t = k % kTileRing;
             if (k >= kTileRing && !wait(&tempty[t], (uint32_t)(((k / kTileRing) - 1) & 1))) { ok = false; break; }
             *reinterpret_cast<int4 *>(&s_trow[t * kTileM + 4 * lane]) = make_int4(rA[0], rA[1], rA[2], rA[3]);
+            {
+                int base_v = 0;
+#pragma unroll
+                for (int w = 0; w < kMaxMaskWords; ++w) {
+                    if (w < MWS) {
+                        *reinterpret_cast<uint4 *>(&s_srm[w * kTileM + 4 * lane]) =
+                            make_uint4(mA[0][w], mA[1][w], mA[2][w], mA[3][w]);
+                        // active offsets in ascending order: lane b writes bit b of this word
+                        if ((tm[w] >> lane) & 1u)
+                            s_tact[base_v + __popc(tm[w] & ((1u << lane) - 1u))] = (uint8_t)(w * 32 + lane);
+                        base_v += __popc(tm[w]);
+                    }
+                }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tfull[t]));
 
-            int w = 0, vnext = 0;
-            uint32_t bits = tm[0];
+            int c0 = 0;                      // first active offset of the next context
             bool first = true;
             while (left > 0) {
                 const int cnt = left < kChunk ? left : kChunk;
                 const int cb = g % kCtxBufs;
                 if (g >= kCtxBufs && !wait(&cempty[cb], (uint32_t)(((g / kCtxBufs) - 1) & 1))) { ok = false; break; }
-                int32_t *dn = &s_n[cb * kChunk * kTileM + 4 * lane];
-                for (int i = 0; i < cnt; ++i) {
-                    int v = 0;
-                    if (!fake) {
-                        if (!use_masks) {
-                            v = vnext++;
-                        } else {
-                            while (bits == 0u && w + 1 < MWS) {
-                                ++w;
-                                bits = sel4(tm[0], tm[1], tm[2], tm[3], w);
-                            }
-                            v = bits ? w * 32 + __ffs(bits) - 1 : 0;
-                            bits &= bits - 1u;
-                        }
-                    }
-                    if (lane == 0) s_act[cb * kChunk + i] = v;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        bool have = rA[j] >= 0 && !fake;
-                        if (have && use_masks)
-                            have = ((sel4(mA[j][0], mA[j][1], mA[j][2], mA[j][3], v >> 5) >> (v & 31)) & 1u) != 0u;
-                        int32_t *d = dn + i * kTileM + j;
-                        if (have) cp_async_4(smem_u32(d), nbr + (int64_t)rA[j] * V + v);
-                        else *d = -1;
+                // P = cnt rounded up to a power of two lanes share one voxel's index row: lane l
+                // loads offset slot i = l % P of rows (32/P)*kk + l/P, so one warp instruction
+                // touches the index rows of 32/P voxels rather than 32.
+                const int lp = cnt > 1 ? 32 - __clz(cnt - 1) : 0;        // log2(P)
+                const int i = lane & ((1 << lp) - 1);
+                int v = 0;
+                if (!fake && i < cnt) v = use_masks ? (int)s_tact[c0 + i] : c0 + i;
+                if (lane < cnt) s_act[cb * kChunk + lane] = v;
+                const uint32_t *rm = &s_srm[(v >> 5) * kTileM];
+                int32_t *dn = &s_n[cb * kTileM * kNPitch + i];
+                auto load_index = [&](int r) {
+                    const int32_t row = s_trow[t * kTileM + r];
+                    bool have = row >= 0 && !fake;
+                    if (have && use_masks) have = ((rm[r] >> (v & 31)) & 1u) != 0u;
+                    int32_t *d = dn + r * kNPitch;
+                    if (have) cp_async_4(smem_u32(d), nbr + (int64_t)row * V + v);
+                    else *d = -1;
+                };
+                if (i < cnt) {
+                    if (lp == 4) {                                       // full contexts: fixed trip count
+#pragma unroll 8
+                        for (int kk = 0; kk < kTileM / 2; ++kk) load_index(2 * kk + (lane >> 4));
+                    } else {
+                        const int rpi = 32 >> lp;                        // rows per warp instruction
+#pragma unroll 4
+                        for (int r = lane >> lp; r < kTileM; r += rpi) load_index(r);
                     }
                 }
                 cp_async_commit();
+                c0 += cnt;
                 left -= cnt;
                 if (lane == 0) s_cinfo[cb] = make_int4(k, cnt, (first ? kCtxFirst : 0) | (left == 0 ? kCtxLast : 0), 0);
                 first = false;
@@ -340,17 +362,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             for (int i = 0; i < cnt && ok; ++i) {
                 const int v = s_act[cb * kChunk + i];
                 int32_t n[LPR];
-                const int32_t *np = &s_n[(cb * kChunk + i) * kTileM + row0];
-                if constexpr (LPR == 8) {
-                    const int4 a = reinterpret_cast<const int4 *>(np)[0], b = reinterpret_cast<const int4 *>(np)[1];
-                    n[0] = a.x; n[1] = a.y; n[2] = a.z; n[3] = a.w; n[4] = b.x; n[5] = b.y; n[6] = b.z; n[7] = b.w;
-                } else if constexpr (LPR == 4) {
-                    const int4 a = reinterpret_cast<const int4 *>(np)[0];
-                    n[0] = a.x; n[1] = a.y; n[2] = a.z; n[3] = a.w;
-                } else {
-                    const int2 a = reinterpret_cast<const int2 *>(np)[0];
-                    n[0] = a.x; n[1] = a.y;
-                }
+                const int32_t *np = &s_n[(cb * kTileM + row0) * kNPitch + i];
+#pragma unroll
+                for (int q = 0; q < LPR; ++q) n[q] = np[q * kNPitch];
 #pragma unroll
                 for (int kc = 0; kc < NKC; ++kc) {
                     const int s = step % S, u = step / S;
