@@ -170,6 +170,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
+    grid_dependency_wait();                  // the map build's order, masks and map
 
     // Tiles are taken from the end of the voxel order first: voxels with the most neighbours
     // sort last, so the tiles with the most active offsets start earliest.
@@ -581,8 +582,10 @@ static int launch_tc(const ConvArgs &a) {
     int grid = sms * occ_cache[dev];
     if (grid > num_tiles) grid = num_tiles;
     if (grid < 1) grid = 1;
-    kern<<<grid, kTcThreads, smem, a.stream>>>(tw, (const T *)a.feats, (const T *)a.bias, a.nbr, a.masks,
-                                               a.order, (T *)a.out, a.M, a.V, a.MW, MWS, num_tiles, a.status);
+    const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kTcThreads), (size_t)smem, a.stream, tw,
+                                      (const T *)a.feats, (const T *)a.bias, a.nbr, a.masks, a.order, (T *)a.out,
+                                      a.M, a.V, a.MW, MWS, num_tiles, a.status);
+    if (le != cudaSuccess) return check_launch("conv_tc_kernel launch");
     return check_launch("conv_tc_kernel");
 }
 

@@ -132,13 +132,12 @@ __device__ __forceinline__ bool table_insert(unsigned long long *table, uint32_t
         unsigned long long *grp = table + g * kGroup;
 #pragma unroll
         for (int i = 0; i < kGroup; ++i) {
-            unsigned long long cur = grp[i];
+            // CAS straight away: at the table's low load it usually succeeds, and on an
+            // occupied slot it returns the occupant for the duplicate test.
+            const unsigned long long cur = atomicCAS(grp + i, 0ull, desired);
             if (cur == 0ull) {
-                cur = atomicCAS(grp + i, 0ull, desired);
-                if (cur == 0ull) {
-                    if (KEY64) atomicMax(vals + g * kGroup + i, row);
-                    return true;
-                }
+                if (KEY64) atomicMax(vals + g * kGroup + i, row);
+                return true;
             }
             const bool same = KEY64 ? (cur == desired) : ((uint32_t)(cur >> 32) == (uint32_t)(desired >> 32));
             if (same) {
@@ -240,6 +239,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     const int64_t i0 = (int64_t)blockIdx.x * kMapThreads;
     const int nvox = (M - i0) < (int64_t)kMapThreads ? (int)(M - i0) : kMapThreads;
     const bool staged = vstride > 0;
+    grid_dependency_wait();                                     // the insert's table and bitmap
 
     for (int v = tid; v < V; v += kMapThreads) {
         const int KhKd = Kh * Kd;
@@ -426,6 +426,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     const int64_t i0 = (int64_t)blockIdx.x * nthr;
     const int nvox = (M - i0) < (int64_t)nthr ? (int)(M - i0) : nthr;
     const bool staged = vstride > 0;
+    grid_dependency_wait();                                     // the insert's table and bitmap
     for (int j = tid; j < kOrderBuckets; j += nthr) s_hist[j] = 0u;
     __syncthreads();
 
@@ -587,6 +588,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     const bool in_z[3] = {c.w - Dd >= 0, true, c.w + Dd < D};
     const uint32_t zbits = (in_z[0] ? 1u : 0u) | 2u | (in_z[2] ? 4u : 0u);
 
+    grid_dependency_wait();                                     // the insert's table and bitmap
     // Phase 1: candidate offsets.
     uint32_t cand = 0;
     if (valid) {
@@ -770,6 +772,7 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
         return r;
     };
 
+    grid_dependency_wait();                                     // the insert's table and bitmap
     // Phase 1: candidate offsets.
     uint32_t cand[4] = {0u, 0u, 0u, 0u};
     const int ncol = Kw * Kh;
@@ -890,6 +893,7 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, uint32_t *cu
     const int tid = threadIdx.x;
     const int64_t i0 = (int64_t)blockIdx.x * (kOrderThreads * kOrderPerThread);
     for (int b = tid; b < kOrderBuckets; b += kOrderThreads) s_cnt[b] = 0u;
+    grid_dependency_wait();                                     // the map kernel's masks and cursors
     __syncthreads();
     uint32_t key[kOrderPerThread], rank[kOrderPerThread];
 #pragma unroll
@@ -1001,9 +1005,10 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         auto k3_fn = bitmap ? map_kernel_k3<true> : map_kernel_k3<false>;
         const int grid = (int)((M + kMapK3Threads - 1) / kMapK3Threads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
-        k3_fn<<<grid, kMapK3Threads, 0, stream>>>(
-            (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, table, bitmap, L.bitmap_words, gmask, shift,
-            neighbor_map, masks, hist, cursor, counter, status);
+        launch_pdl(k3_fn, dim3(grid), dim3(kMapK3Threads), 0, stream,
+                   (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, (const unsigned long long *)table,
+                   (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
+                   cursor, counter, status);
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
         const size_t smem = ((size_t)kMapColsThreads * V * sizeof(int32_t) + 15) / 16 * 16;
         static bool cols_attr_done = false;
@@ -1013,9 +1018,10 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         }
         const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
-        map_kernel_cols<<<grid, kMapColsThreads, smem, stream>>>(
-            (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, table, bitmap, L.bitmap_words,
-            gmask, shift, neighbor_map, masks, hist, cursor, counter, status);
+        launch_pdl(map_kernel_cols, dim3(grid), dim3(kMapColsThreads), smem, stream,
+                   (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW,
+                   (const unsigned long long *)table, (const uint32_t *)bitmap, L.bitmap_words, gmask,
+                   shift, neighbor_map, masks, hist, cursor, counter, status);
     } else if (bitmap && Kd <= kColBatchMax) {
         // 256 voxels per block while their staged rows fit in 64 KB, else 128.
         const int nthr = ((size_t)kMapBmMaxThreads * (V | 1) * 4 <= 64 * 1024) ? kMapBmMaxThreads : 128;
@@ -1059,7 +1065,8 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     const int per_block = kOrderThreads * kOrderPerThread;
     const int ord_grid = (int)((M + per_block - 1) / per_block);
     stage_mark(SPCONV_STAGE_ORDER, 0, stream);
-    order_kernel<<<ord_grid, kOrderThreads, 0, stream>>>(masks, M, MW, cursor, order, status);
+    launch_pdl(order_kernel, dim3(ord_grid), dim3(kOrderThreads), 0, stream, (const uint32_t *)masks, M, MW,
+               cursor, order, status);
     if (int rc = check_launch("order_kernel")) return rc;
     stage_mark(SPCONV_STAGE_ORDER, 1, stream);
     return SPCONV_OK;
