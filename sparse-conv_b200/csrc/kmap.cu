@@ -60,9 +60,11 @@ struct WsLayout {
     int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, counter = 0, total = 0;
 };
 
-// Grids of at most 2^28 cells (a 32 MB bitmap) get an occupancy bitmap, one bit per cell,
-// that screens neighbour probes: a clear bit settles a probe with one cached 4-byte load.
-constexpr long double kBitmapMaxCells = 268435456.0L;
+// Grids of at most 2^30 cells (a 128 MB bitmap, cleared with the table) get an occupancy
+// bitmap, one bit per cell, that screens neighbour probes: a clear bit settles a probe with
+// one cached 4-byte load. Clearing 128 MB costs ~40 us; without the bitmap every absent
+// neighbour of a surface scene (about half of 26) probes the table.
+constexpr long double kBitmapMaxCells = 1073741824.0L;
 static int64_t bitmap_words_for(int batch, int W, int H, int D) {
     const long double vol = (long double)batch * W * H * D;
     if (vol > kBitmapMaxCells) return 0;

@@ -62,11 +62,11 @@ def test_mask_words(lib):
 
 def test_workspace_bytes(lib):
     cap = lib.spconv_hashmap_capacity(1000)
-    # <= 2^28 cells: table + a one-bit-per-cell occupancy bitmap
+    # <= 2^30 cells: table + a one-bit-per-cell occupancy bitmap
     small_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 4, 128, 128, 128)
     assert small_grid >= 8 * cap + 4 * 128 ** 3 // 8
-    # 2^28 < cells < 2^32: table only
-    mid_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 8, 512, 512, 512)
+    # 2^30 < cells < 2^32: table only
+    mid_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 16, 512, 512, 512)
     assert 8 * cap <= mid_grid < 8 * cap + 64 * 1024
     # >= 2^32 cells: 64-bit keys add a row array
     big_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 2, 2048, 2048, 1024)

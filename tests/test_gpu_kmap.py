@@ -114,7 +114,7 @@ def test_non_default_stream():
 
 @pytest.mark.parametrize("name", ["rand3", "rand5", "aniso", "dense3"])
 def test_hash_only_path_matches_bitmap_path(name):
-    """Grids of <= 2^28 cells screen probes with an occupancy bitmap when the workspace has
+    """Grids of <= 2^30 cells screen probes with an occupancy bitmap when the workspace has
     room for it; with a workspace too small for the bitmap the build probes the hash table
     alone. Both must give the oracle's map."""
     coords, shape, ks, dil = gpu_cases.small_cases()[name]
