@@ -60,7 +60,7 @@ struct TcCfg {
     static constexpr int kBBytes = CO * kRowBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kNBytes = kCtxBufs * kTileM * kNPitch * 4;
-    static constexpr int kSchedBytes = kMaxMaskWords * kTileM * 4 + kTileM;   // row masks, active list
+    static constexpr int kSchedBytes = kTileM;                               // active-offset list
     static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kChunk * 4 + kCtxBufs * 16 +
                                        kTileRing * kTileM * 4 + kMaxStages * 4 + 40 * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
@@ -72,8 +72,7 @@ struct TcCfg {
     static constexpr int kOffA = 0;
     static constexpr int kOffB = kOffA + kStages * kABytes;
     static constexpr int kOffN = kOffB + kStages * kBBytes;
-    static constexpr int kOffSrm = kOffN + kNBytes;
-    static constexpr int kOffTact = kOffSrm + kMaxMaskWords * kTileM * 4;
+    static constexpr int kOffTact = kOffN + kNBytes;
     static constexpr int kOffAct = kOffTact + kTileM;
     static constexpr int kOffCInfo = kOffAct + kCtxBufs * kChunk * 4;
     static constexpr int kOffTRow = kOffCInfo + kCtxBufs * 16;
@@ -128,7 +127,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t sA = smem_u32(base + Cfg::kOffA), sB = smem_u32(base + Cfg::kOffB);
     int32_t *s_n = reinterpret_cast<int32_t *>(base + Cfg::kOffN);        // [ctx][row][kNPitch]
-    uint32_t *s_srm = reinterpret_cast<uint32_t *>(base + Cfg::kOffSrm);  // scheduler: [word][row] masks
     uint8_t *s_tact = base + Cfg::kOffTact;                               // scheduler: tile's active offsets
     int32_t *s_act = reinterpret_cast<int32_t *>(base + Cfg::kOffAct);    // [ctx][i] -> v
     int4 *s_cinfo = reinterpret_cast<int4 *>(base + Cfg::kOffCInfo);      // [ctx] {k, cnt, flags}
@@ -247,8 +245,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
 #pragma unroll
                 for (int w = 0; w < kMaxMaskWords; ++w) {
                     if (w < MWS) {
-                        *reinterpret_cast<uint4 *>(&s_srm[w * kTileM + 4 * lane]) =
-                            make_uint4(mA[0][w], mA[1][w], mA[2][w], mA[3][w]);
                         // active offsets in ascending order: lane b writes bit b of this word
                         if ((tm[w] >> lane) & 1u)
                             s_tact[base_v + __popc(tm[w] & ((1u << lane) - 1u))] = (uint8_t)(w * 32 + lane);
@@ -273,14 +269,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 int v = 0;
                 if (!fake && i < cnt) v = use_masks ? (int)s_tact[c0 + i] : c0 + i;
                 if (lane < cnt) s_act[cb * kChunk + lane] = v;
-                const uint32_t *rm = &s_srm[(v >> 5) * kTileM];
                 int32_t *dn = &s_n[cb * kTileM * kNPitch + i];
+                // A row's map entry is -1 where its mask bit is clear, so no per-row mask test is
+                // needed: the lanes of one row fetch the same cache line(s) either way.
+                const int32_t *nv = nbr + v;
                 auto load_index = [&](int r) {
                     const int32_t row = s_trow[t * kTileM + r];
-                    bool have = row >= 0 && !fake;
-                    if (have && use_masks) have = ((rm[r] >> (v & 31)) & 1u) != 0u;
                     int32_t *d = dn + r * kNPitch;
-                    if (have) cp_async_4(smem_u32(d), nbr + (int64_t)row * V + v);
+                    if (row >= 0 && !fake) cp_async_4(smem_u32(d), nv + (int64_t)row * V);
                     else *d = -1;
                 };
                 if (i < cnt) {
