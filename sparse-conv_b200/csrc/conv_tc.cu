@@ -41,6 +41,9 @@ constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTileM = 128;
 constexpr int kChunk = 16;          // active offsets per context
 constexpr int kNPitch = kChunk + 1; // words per row in a context buffer (conflict-free both ways)
+constexpr int kRowWindow = 32;      // words per staged index row: a 128-byte aligned window
+constexpr int kRowsMaxV = 28;       // V for which a voxel's whole index row fits one window
+constexpr int kActMax = 32;         // active offsets per context buffer
 constexpr int kCtxBufs = 3;
 constexpr int kTileRing = 4;        // tiles whose rows the epilogue may still need
 constexpr int kMaxMaskWords = 4;    // offset masks are used for V <= 128 (else all offsets run)
@@ -48,7 +51,10 @@ constexpr int kMaxStages = 8;
 constexpr int kGatherWarps = 4;
 constexpr int kWarpSched = 0, kWarpGather = 1, kWarpMma = 5, kWarpEpi = 6;
 constexpr uint32_t kInfoFirst = 1u << 30, kInfoLast = 1u << 31, kInfoEnd = 0x3fffffffu;
-constexpr int kCtxFirst = 1, kCtxLast = 2, kCtxEnd = 8;
+constexpr int kCtxFirst = 1, kCtxLast = 2, kCtxRows = 4, kCtxEnd = 8;
+// Tiles with more active offsets than this stage whole index rows (when V <= kRowsMaxV): one
+// 128-byte window per voxel costs about what a context of 5..8 offsets does.
+constexpr int kRowsMinAct = 9;
 
 template <int CI, int CO>
 struct TcCfg {
@@ -59,12 +65,18 @@ struct TcCfg {
     static constexpr int kABytes = kTileM * kRowBytes;
     static constexpr int kBBytes = CO * kRowBytes;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kNBytes = kCtxBufs * kTileM * kNPitch * 4;
-    static constexpr int kSchedBytes = kTileM;                               // active-offset list
-    static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kChunk * 4 + kCtxBufs * 16 +
+    // Whole-row staging pays where the gatherers are fast relative to the index loads (rows of
+    // at most 64 bytes); wider rows keep the smaller per-offset buffers and one more stage.
+    static constexpr bool kRows = KC <= 32;
+    static constexpr int kBufWords = kTileM * (kRows ? kRowWindow : kNPitch);   // one context buffer
+    static constexpr int kNBytes = kCtxBufs * kBufWords * 4;
+    static_assert(kRowWindow >= kNPitch, "context buffer");
+    static constexpr int kSchedBytes = kTileM + kCtxBufs * kTileM;           // active list, row shifts
+    static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kActMax * 4 + kCtxBufs * 16 +
                                        kTileRing * kTileM * 4 + kMaxStages * 4 + 40 * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
     static constexpr int kBudget = kStageBytes <= 12 * 1024 ? 110 * 1024 : 219 * 1024;
+    static constexpr int kMinBlocks = kStageBytes <= 12 * 1024 ? 2 : 1;   // registers for two CTAs
     static constexpr int kStagesFit = (kBudget - kFixedBytes - 1024) / kStageBytes;
     static constexpr int kStages = kStagesFit > kMaxStages ? kMaxStages : (kStagesFit < 3 ? 3 : kStagesFit);
     static constexpr int kDepth = kStages - 1;             // cp.async groups in flight per gatherer
@@ -73,8 +85,9 @@ struct TcCfg {
     static constexpr int kOffB = kOffA + kStages * kABytes;
     static constexpr int kOffN = kOffB + kStages * kBBytes;
     static constexpr int kOffTact = kOffN + kNBytes;
-    static constexpr int kOffAct = kOffTact + kTileM;
-    static constexpr int kOffCInfo = kOffAct + kCtxBufs * kChunk * 4;
+    static constexpr int kOffMis = kOffTact + kTileM;
+    static constexpr int kOffAct = kOffMis + kCtxBufs * kTileM;
+    static constexpr int kOffCInfo = kOffAct + kCtxBufs * kActMax * 4;
     static constexpr int kOffTRow = kOffCInfo + kCtxBufs * 16;
     static constexpr int kOffInfo = kOffTRow + kTileRing * kTileM * 4;
     static constexpr int kOffBar = kOffInfo + kMaxStages * 4;
@@ -114,11 +127,11 @@ __device__ __forceinline__ uint32_t sel4(uint32_t a, uint32_t b, uint32_t c, uin
 }
 
 template <int CI, int CO, typename T>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, TcCfg<CI, CO>::kMinBlocks)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__ feats,
                const T *__restrict__ bias, const int32_t *__restrict__ nbr,
                const uint32_t *__restrict__ masks, const int32_t *__restrict__ order,
-               T *__restrict__ out, int64_t M, int V, int MW, int MWS, int num_tiles,
+               T *__restrict__ out, int64_t M, int V, int MW, int MWS, int num_tiles, int row_mode,
                int32_t *status) {
     using Cfg = TcCfg<CI, CO>;
     constexpr int S = Cfg::kStages, KC = Cfg::KC, NKC = Cfg::NKC, RB = Cfg::kRowBytes;
@@ -126,7 +139,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t sA = smem_u32(base + Cfg::kOffA), sB = smem_u32(base + Cfg::kOffB);
-    int32_t *s_n = reinterpret_cast<int32_t *>(base + Cfg::kOffN);        // [ctx][row][kNPitch]
+    int32_t *s_n = reinterpret_cast<int32_t *>(base + Cfg::kOffN);        // [ctx][kBufWords]: rows at pitch kNPitch or kRowWindow
+    uint8_t *s_mis = base + Cfg::kOffMis;                                 // [ctx][row]: word rotation of the staged row
     uint8_t *s_tact = base + Cfg::kOffTact;                               // scheduler: tile's active offsets
     int32_t *s_act = reinterpret_cast<int32_t *>(base + Cfg::kOffAct);    // [ctx][i] -> v
     int4 *s_cinfo = reinterpret_cast<int4 *>(base + Cfg::kOffCInfo);      // [ctx] {k, cnt, flags}
@@ -257,6 +271,52 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
 
             int c0 = 0;                      // first active offset of the next context
             bool first = true;
+            if (Cfg::kRows && row_mode && nact >= kRowsMinAct) {
+                // One context per tile: stage every voxel's whole index row (V <= 28 words) as a
+                // 128-byte aligned window, 8 lanes per row, 16 bytes per lane. Chunk c of row r
+                // lands in slot (c + rot) % 8, rot = (r + r/8) % 8, so word j of the row sits at
+                // (j + shift + 4 rot) % 32 with shift = the row's offset in its window; that
+                // rotation is kept per row. Rows without a voxel hold -1 throughout.
+                const int cb = g % kCtxBufs;
+                if (g >= kCtxBufs && !wait(&cempty[cb], (uint32_t)(((g / kCtxBufs) - 1) & 1))) { ok = false; break; }
+                const int cnt = left;
+                if (lane < cnt) s_act[cb * kActMax + lane] = fake ? 0 : (use_masks ? (int)s_tact[lane] : lane);
+                const char *nb = reinterpret_cast<const char *>(nbr);
+                const int64_t nbytes = M * (int64_t)V * 4;
+                const int c = lane & 7, rs = lane >> 3;
+#pragma unroll 4
+                for (int it = 0; it < kTileM / 4; ++it) {
+                    const int r = 4 * it + rs;
+                    const int32_t row = s_trow[t * kTileM + r];
+                    int32_t *wrow = &s_n[(cb * kTileM + r) * kRowWindow];
+                    if (row < 0 || fake) {
+                        if (c == 0) s_mis[cb * kTileM + r] = 0;
+                        *reinterpret_cast<int4 *>(wrow + 4 * c) = make_int4(-1, -1, -1, -1);
+                        continue;
+                    }
+                    const int rot = (r + (r >> 3)) & 7;
+                    const int64_t a0 = (int64_t)row * V * 4;
+                    const int64_t ws = a0 & ~(int64_t)15;
+                    const int shift = (int)(a0 - ws) >> 2;
+                    if (c == 0) s_mis[cb * kTileM + r] = (uint8_t)((shift + 4 * rot) & 31);
+                    if (c < (shift * 4 + V * 4 + 15) >> 4) {
+                        const int64_t so = ws + 16 * c;
+                        const uint32_t dst = smem_u32(wrow + ((c + rot) & 7) * 4);
+                        if (so + 16 <= nbytes) {
+                            cp_async_16(dst, nb + so, 16u);
+                        } else {                 // the map's last bytes: word by word, in bounds
+                            for (int q = 0; q < 4; ++q)
+                                if (so + 4 * q + 4 <= nbytes) cp_async_4(dst + 4 * q, nb + so + 4 * q);
+                        }
+                    }
+                }
+                cp_async_commit();
+                left = 0;
+                if (lane == 0) s_cinfo[cb] = make_int4(k, cnt, kCtxFirst | kCtxLast | kCtxRows, 0);
+                publish_pending(false);      // the previous tile's rows have landed
+                pend = cb;
+                ++g;
+            }
             while (left > 0) {
                 const int cnt = left < kChunk ? left : kChunk;
                 const int cb = g % kCtxBufs;
@@ -268,8 +328,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 const int i = lane & ((1 << lp) - 1);
                 int v = 0;
                 if (!fake && i < cnt) v = use_masks ? (int)s_tact[c0 + i] : c0 + i;
-                if (lane < cnt) s_act[cb * kChunk + lane] = v;
-                int32_t *dn = &s_n[cb * kTileM * kNPitch + i];
+                if (lane < cnt) s_act[cb * kActMax + lane] = v;
+                int32_t *dn = &s_n[cb * Cfg::kBufWords + i];
                 // A row's map entry is -1 where its mask bit is clear, so no per-row mask test is
                 // needed: the lanes of one row fetch the same cache line(s) either way.
                 const int32_t *nv = nbr + v;
@@ -356,12 +416,31 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             if (ci.z & kCtxEnd) break;
             const int k = ci.x, cnt = ci.y;
             const bool cfirst = (ci.z & kCtxFirst) != 0, clast = (ci.z & kCtxLast) != 0;
-            for (int i = 0; i < cnt && ok; ++i) {
-                const int v = s_act[cb * kChunk + i];
-                int32_t n[LPR];
-                const int32_t *np = &s_n[(cb * kTileM + row0) * kNPitch + i];
+            const bool crows = (ci.z & kCtxRows) != 0;
+            // row mode: the rotations of this lane's LPR rows, one byte each
+            uint32_t rotw[(LPR + 3) / 4];
+            if (Cfg::kRows && crows) {
+                if constexpr (LPR >= 4) {
 #pragma unroll
-                for (int q = 0; q < LPR; ++q) n[q] = np[q * kNPitch];
+                    for (int w = 0; w < LPR / 4; ++w)
+                        rotw[w] = reinterpret_cast<const uint32_t *>(s_mis + cb * kTileM + row0)[w];
+                } else {
+                    rotw[0] = *reinterpret_cast<const uint16_t *>(s_mis + cb * kTileM + row0);
+                }
+            }
+            const int32_t *rowp = &s_n[(cb * kTileM + row0) * kRowWindow];
+            for (int i = 0; i < cnt && ok; ++i) {
+                const int v = s_act[cb * kActMax + i];
+                int32_t n[LPR];
+                if (Cfg::kRows && crows) {
+#pragma unroll
+                    for (int q = 0; q < LPR; ++q)
+                        n[q] = rowp[q * kRowWindow + ((v + (int)(rotw[q >> 2] >> (8 * (q & 3)))) & 31)];
+                } else {
+                    const int32_t *np = &s_n[cb * Cfg::kBufWords + row0 * kNPitch + i];
+#pragma unroll
+                    for (int q = 0; q < LPR; ++q) n[q] = np[q * kNPitch];
+                }
 #pragma unroll
                 for (int kc = 0; kc < NKC; ++kc) {
                     const int s = step % S, u = step / S;
@@ -578,9 +657,11 @@ static int launch_tc(const ConvArgs &a) {
     int grid = sms * occ_cache[dev];
     if (grid > num_tiles) grid = num_tiles;
     if (grid < 1) grid = 1;
+    // Whole index rows are staged when one fits a 128-byte window and the map is 16-byte aligned.
+    const int row_mode = (a.V <= kRowsMaxV && ((uintptr_t)a.nbr & 15u) == 0) ? 1 : 0;
     const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kTcThreads), (size_t)smem, a.stream, tw,
                                       (const T *)a.feats, (const T *)a.bias, a.nbr, a.masks, a.order, (T *)a.out,
-                                      a.M, a.V, a.MW, MWS, num_tiles, a.status);
+                                      a.M, a.V, a.MW, MWS, num_tiles, row_mode, a.status);
     if (le != cudaSuccess) return check_launch("conv_tc_kernel launch");
     return check_launch("conv_tc_kernel");
 }

@@ -41,6 +41,17 @@ def small_cases():
     return cases
 
 
+def mixed_density_coords(seed=9):
+    """Dense blocks (tiles with most of the 27 offsets active) beside scattered voxels (tiles
+    with one or two): both index-staging modes of the tensor-core conv run in one launch."""
+    rng = np.random.default_rng(seed)
+    B, R = 2, 40
+    occ = rng.random((B, R, R, R)) < 0.01
+    occ[0, 4:16, 4:16, 4:16] |= rng.random((12, 12, 12)) < 0.9
+    occ[1, 20:34, 10:20, 25:39] |= rng.random((14, 10, 14)) < 0.7
+    return np.ascontiguousarray(np.argwhere(occ).astype(np.int32)), (B, 1, R, R, R)
+
+
 @functools.lru_cache(maxsize=None)
 def workload(name):
     from sparseconv import synthetic

@@ -60,6 +60,21 @@ def test_conv_matches_f64_oracle(kernel, dtype, ci, co, case):
     np.testing.assert_allclose(got, ref, **TOL[dtype])
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("ci,co", [(16, 16), (32, 32), (64, 64), (128, 128)])
+def test_tcgen05_mixed_density(dtype, ci, co):
+    """Tiles of dense blocks and of isolated voxels in one launch (whole index rows staged for
+    the former, per-offset contexts for the latter)."""
+    coords, shape = gpu_cases.mixed_density_coords()
+    N, _C, W, H, D = shape
+    nbr, masks, order = _native.build_neighbor_map(torch.from_numpy(coords).cuda(), N, W, H, D,
+                                                   (3, 3, 3), (1, 1, 1))
+    feats, weight, bias = _inputs(ci + 3 * co, coords.shape[0], ci, co, nbr.shape[1], dtype, with_bias=True)
+    got = _gpu_conv(feats, weight, bias, nbr, masks, order, _native.KERNEL_TCGEN05)
+    ref = _oracle(feats, nbr.cpu().numpy().view(np.uint32), weight, bias)
+    np.testing.assert_allclose(got, ref, **TOL[dtype])
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("ci,co", [(3, 3), (3, 8), (48, 24), (16, 16)])
 @pytest.mark.parametrize("case", sorted(gpu_cases.small_cases()))
