@@ -104,6 +104,15 @@ __device__ __forceinline__ void grid_dependency_wait() {
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
 }
 
+// Lets the next kernel on the stream (if launched with launch_pdl) start its blocks now
+// instead of when this grid exits. Safe at any point: the next kernel still waits, in
+// grid_dependency_wait(), for this whole grid to complete and its writes to be visible; it
+// starts only once every block of this grid has made the call or exited, so its waiting
+// blocks never hold resources this grid's blocks still need.
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t stream, Args... args) {

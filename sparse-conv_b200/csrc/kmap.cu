@@ -34,6 +34,14 @@ constexpr int kOrderBuckets = 4096;    // 16 popcount classes x 256 mask-hash bu
 constexpr int kMapThreads = 128;      // one thread per voxel
 constexpr int kOrderThreads = 256;
 constexpr int kOrderPerThread = 2;     // voxels per thread in order_kernel
+// Radix-sort order (kernels of at most kSortMaxV offsets, at least kSortMinVoxels voxels):
+// tiles of kSortTile voxels, 8-bit digits, keys of at most 31 bits.
+constexpr int kSortThreads = 512;
+constexpr int kSortWarpItems = 256;                                  // 8 rounds of 32 per warp
+constexpr int kSortTile = (kSortThreads / 32) * kSortWarpItems;      // 4096
+constexpr int kSortMaxPasses = 4;
+constexpr int kSortMaxV = 27;
+constexpr int64_t kSortMinVoxels = 1 << 19;
 constexpr int kMaxKernelVolume = 1024;
 
 static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
@@ -58,6 +66,8 @@ struct WsLayout {
     bool key64 = false;
     int64_t bitmap_words = 0;
     int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, counter = 0, total = 0;
+    int sort_tiles = 0;            // > 0: room for the radix-sort order (keys alias the table)
+    int64_t sort_counts = 0;       // [kSortMaxPasses][256][sort_tiles] + [kSortMaxPasses][256] totals
 };
 
 // Grids of at most 2^30 cells (a 128 MB bitmap, cleared with the table) get an occupancy
@@ -88,6 +98,13 @@ static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
     L.hist = off; off += align256(kOrderBuckets * 4);
     L.cursor = off; off += align256(kOrderBuckets * 4);
     L.counter = off; off += 256;
+    if (M >= kSortMinVoxels) {
+        // Sort keys and values (4 x M words) reuse the table, dead once the map is built:
+        // its capacity is at least 2M slots of 8 bytes.
+        L.sort_tiles = (int)((M + kSortTile - 1) / kSortTile);
+        L.sort_counts = off;
+        off += align256((int64_t)kSortMaxPasses * 256 * (L.sort_tiles + 1) * 4);
+    }
     L.total = off;
     return L;
 }
@@ -196,6 +213,7 @@ __global__ void __launch_bounds__(256)
 insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, int D,
               unsigned long long *table, uint32_t *vals, uint32_t *bitmap, uint64_t gmask,
               uint32_t shift, int32_t *status) {
+    grid_launch_dependents();                                   // the map kernel's setup overlaps this
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = __ldg(coords + i);
@@ -242,6 +260,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     const int nvox = (M - i0) < (int64_t)kMapThreads ? (int)(M - i0) : kMapThreads;
     const bool staged = vstride > 0;
     grid_dependency_wait();                                     // the insert's table and bitmap
+    grid_launch_dependents();
 
     for (int v = tid; v < V; v += kMapThreads) {
         const int KhKd = Kh * Kd;
@@ -322,7 +341,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
         const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
         const uint32_t key = cls * 256u + (h & 255u);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
-        if (valid) aggregated_inc(s_hist, key, active);
+        if (valid && hist) aggregated_inc(s_hist, key, active);
     }
     __syncthreads();
 
@@ -338,6 +357,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             if (v >= V) { v -= V; ++il; }
         }
     }
+    if (hist == nullptr) return;                                // radix-sort order: no histogram
     for (int b = tid; b < kOrderBuckets; b += kMapThreads)
         if (s_hist[b]) atomicAdd(hist + b, s_hist[b]);
 
@@ -429,6 +449,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     const int nvox = (M - i0) < (int64_t)nthr ? (int)(M - i0) : nthr;
     const bool staged = vstride > 0;
     grid_dependency_wait();                                     // the insert's table and bitmap
+    grid_launch_dependents();
     for (int j = tid; j < kOrderBuckets; j += nthr) s_hist[j] = 0u;
     __syncthreads();
 
@@ -518,7 +539,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
         const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
         const uint32_t k = cls * 256u + (h & 255u);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
-        if (valid) aggregated_inc(s_hist, k, active);
+        if (valid && hist) aggregated_inc(s_hist, k, active);
     }
     __syncthreads();
 
@@ -542,7 +563,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             }
         }
     }
-    block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+    if (hist) block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -591,6 +612,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     const uint32_t zbits = (in_z[0] ? 1u : 0u) | 2u | (in_z[2] ? 4u : 0u);
 
     grid_dependency_wait();                                     // the insert's table and bitmap
+    grid_launch_dependents();
     // Phase 1: candidate offsets.
     uint32_t cand = 0;
     if (valid) {
@@ -682,7 +704,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
         const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
         const uint32_t k = cls * 256u + (h & 255u);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
-        if (valid) aggregated_inc(s_hist, k, active);
+        if (valid && hist) aggregated_inc(s_hist, k, active);
     }
     __syncthreads();
     {
@@ -695,7 +717,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
         for (int e = tid; e < n4; e += kMapK3Threads) dst[e] = src[e];
         for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
     }
-    block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+    if (hist) block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -775,6 +797,7 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     };
 
     grid_dependency_wait();                                     // the insert's table and bitmap
+    grid_launch_dependents();
     // Phase 1: candidate offsets.
     uint32_t cand[4] = {0u, 0u, 0u, 0u};
     const int ncol = Kw * Kh;
@@ -865,7 +888,7 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
         const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
         const uint32_t k = cls * 256u + (h & 255u);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
-        if (valid) aggregated_inc(s_hist, k, active);
+        if (valid && hist) aggregated_inc(s_hist, k, active);
     }
     __syncthreads();
     {
@@ -881,7 +904,7 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             for (int e = tid; e < total; e += kMapColsThreads) out[e] = s_stage[e];
         }
     }
-    block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+    if (hist) block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -896,6 +919,7 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, uint32_t *cu
     const int64_t i0 = (int64_t)blockIdx.x * (kOrderThreads * kOrderPerThread);
     for (int b = tid; b < kOrderBuckets; b += kOrderThreads) s_cnt[b] = 0u;
     grid_dependency_wait();                                     // the map kernel's masks and cursors
+    grid_launch_dependents();
     __syncthreads();
     uint32_t key[kOrderPerThread], rank[kOrderPerThread];
 #pragma unroll
@@ -924,6 +948,203 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, uint32_t *cu
             const uint32_t pos = s_base[key[k]] + rank[k];
             if (pos < (uint64_t)M) order[pos] = (int32_t)i;
             else raise_status(status, SPCONV_STATUS_TABLE_FULL);   // inconsistent histogram
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// 3b. Order by a stable LSD radix sort of the voxels' mask keys (V <= 27, M >= 2^19).
+//     key = neighbour-count class (4 bits: min(popcount - 1, 15)) above the top 20 bits of
+//     the mask without its centre bit (all V - 1 bits when V <= 21). The order groups voxels
+//     by class and, inside a class, by the mask read as a number: masks next to each other
+//     share their high offsets, so a 128-voxel tile of the order needs few offsets beyond its
+//     voxels' own. Equal keys keep input order (the (b,x,y,z) order of the coordinates), so
+//     their feature rows are gathered with spatial locality.
+//     Per 8-bit digit pass: sort_count_kernel counts each 4096-key tile's digits,
+//     sort_scan_kernel (one block per digit) scans the counts over tiles, and
+//     sort_scatter_kernel ranks each tile's keys stably (lanes with equal digits found by
+//     eight ballots, per-warp digit counters, warps in input order) and writes them to their
+//     sorted positions.
+// ---------------------------------------------------------------------------------------
+constexpr int kSortCompBits = 20;
+
+__device__ __host__ __forceinline__ int order_key_drop(int V) {
+    return V - 1 > kSortCompBits ? V - 1 - kSortCompBits : 0;
+}
+
+__device__ __forceinline__ uint32_t order_key(uint32_t m, int V) {
+    const int c = V / 2, drop = order_key_drop(V);
+    m &= (1u << V) - 1u;                                        // V <= 27
+    const uint32_t comp = (m & ((1u << c) - 1u)) | ((m >> (c + 1)) << c);
+    const uint32_t pc = (uint32_t)__popc(m);
+    const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+    return (cls << (V - 1 - drop)) | (comp >> drop);
+}
+
+// Number of 8-bit passes for the keys of a V-offset kernel.
+static int sort_passes(int V) {
+    return (4 + V - 1 - order_key_drop(V) + 7) / 8;
+}
+
+// Lanes of the warp whose 8-bit digit equals this lane's, among `active`.
+__device__ __forceinline__ uint32_t digit_peers(uint32_t d, uint32_t active) {
+    uint32_t peers = active;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        const bool bit = (d >> b) & 1u;
+        const uint32_t bb = __ballot_sync(0xffffffffu, bit);
+        peers &= bit ? bb : ~bb;
+    }
+    return peers;
+}
+
+template <bool FIRST>
+__global__ void __launch_bounds__(kSortThreads)
+sort_count_kernel(const uint32_t *__restrict__ masks, int V, const uint32_t *__restrict__ keys,
+                  int64_t M, int ntiles, int shift, uint32_t *__restrict__ counts) {
+    __shared__ uint32_t s_cnt[256];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < 256) s_cnt[tid] = 0u;
+    grid_dependency_wait();                                     // the masks / the previous pass's keys
+    grid_launch_dependents();
+    __syncthreads();
+    const int64_t e0 = (int64_t)blockIdx.x * kSortTile + warp * kSortWarpItems + lane;
+    uint32_t d[kSortWarpItems / 32];
+#pragma unroll
+    for (int k = 0; k < kSortWarpItems / 32; ++k) {
+        const int64_t e = e0 + 32 * k;
+        d[k] = 0xffffffffu;
+        if (e < M) d[k] = ((FIRST ? order_key(__ldg(masks + e), V) : __ldg(keys + e)) >> shift) & 255u;
+    }
+#pragma unroll
+    for (int k = 0; k < kSortWarpItems / 32; ++k) {
+        const bool valid = d[k] != 0xffffffffu;
+        const uint32_t peers = digit_peers(d[k], __ballot_sync(0xffffffffu, valid));
+        if (valid && lane == __ffs(peers) - 1) atomicAdd(&s_cnt[d[k]], (uint32_t)__popc(peers));
+    }
+    __syncthreads();
+    if (tid < 256) counts[(int64_t)tid * ntiles + blockIdx.x] = s_cnt[tid];
+}
+
+// Exclusive block scan of one value per thread (blockDim.x = kSortThreads); also returns
+// the block total. Uses s_warp[kSortThreads / 32 + 1].
+__device__ __forceinline__ uint32_t sort_block_scan(uint32_t x, uint32_t *s_warp, uint32_t &total) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int kWarps = kSortThreads / 32;
+    uint32_t incl = x;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += n;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t w = lane < kWarps ? s_warp[lane] : 0u;
+        uint32_t wi = w;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t n = __shfl_up_sync(0xffffffffu, wi, d);
+            if (lane >= d) wi += n;
+        }
+        if (lane < kWarps) s_warp[lane] = wi - w;
+        if (lane == kWarps - 1) s_warp[kWarps] = wi;
+    }
+    __syncthreads();
+    const uint32_t r = s_warp[warp] + incl - x;
+    total = s_warp[kWarps];
+    __syncthreads();                                            // s_warp reusable
+    return r;
+}
+
+// counts[d][0..ntiles) -> exclusive prefix over tiles, in place; totals[d] = the digit's count.
+__global__ void __launch_bounds__(kSortThreads)
+sort_scan_kernel(uint32_t *__restrict__ counts, int ntiles, uint32_t *__restrict__ totals) {
+    __shared__ uint32_t s_warp[kSortThreads / 32 + 1];
+    uint32_t *row = counts + (int64_t)blockIdx.x * ntiles;
+    grid_dependency_wait();                                     // counts of this pass
+    grid_launch_dependents();
+    uint32_t carry = 0;
+    for (int base = 0; base < ntiles; base += kSortThreads) {
+        const int t = base + (int)threadIdx.x;
+        const uint32_t x = t < ntiles ? row[t] : 0u;
+        uint32_t tot;
+        const uint32_t ex = sort_block_scan(x, s_warp, tot);
+        if (t < ntiles) row[t] = carry + ex;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) totals[blockIdx.x] = carry;
+}
+
+template <bool FIRST, bool LAST>
+__global__ void __launch_bounds__(kSortThreads)
+sort_scatter_kernel(const uint32_t *__restrict__ masks, int V, const uint32_t *__restrict__ keys_in,
+                    const uint32_t *__restrict__ vals_in, int64_t M, int ntiles, int shift,
+                    const uint32_t *__restrict__ offsets, const uint32_t *__restrict__ totals,
+                    uint32_t *__restrict__ keys_out, uint32_t *__restrict__ vals_out, int32_t *status) {
+    constexpr int kWarps = kSortThreads / 32, kRounds = kSortWarpItems / 32;
+    __shared__ uint32_t s_wcnt[kWarps][256];                    // per-warp digit counts, then bases
+    __shared__ uint32_t s_dbase[256];
+    __shared__ uint32_t s_warp[kWarps + 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tile = blockIdx.x;
+    for (int j = tid; j < kWarps * 256; j += kSortThreads) (&s_wcnt[0][0])[j] = 0u;
+    grid_dependency_wait();                                     // this pass's scanned counts
+    grid_launch_dependents();
+    __syncthreads();
+
+    const int64_t e0 = (int64_t)tile * kSortTile + warp * kSortWarpItems + lane;
+    uint32_t key[kRounds], val[kRounds], loc[kRounds];
+    const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+    for (int k = 0; k < kRounds; ++k) {
+        const int64_t e = e0 + 32 * k;
+        key[k] = 0u;
+        val[k] = 0xffffffffu;                                   // marks lanes past the end
+        if (e < M) {
+            if (FIRST) { key[k] = order_key(__ldg(masks + e), V); val[k] = (uint32_t)e; }
+            else { key[k] = __ldg(keys_in + e); val[k] = __ldg(vals_in + e); }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kRounds; ++k) {
+        const bool valid = val[k] != 0xffffffffu;
+        const uint32_t d = (key[k] >> shift) & 255u;
+        const uint32_t peers = digit_peers(d, __ballot_sync(0xffffffffu, valid));
+        const uint32_t before = valid ? s_wcnt[warp][d] : 0u;
+        __syncwarp();
+        if (valid && lane == __ffs(peers) - 1) s_wcnt[warp][d] = before + (uint32_t)__popc(peers);
+        __syncwarp();
+        loc[k] = before + (uint32_t)__popc(peers & lt);
+    }
+    __syncthreads();
+    // Per digit: warps' exclusive prefix in warp order; digit start = all smaller digits of
+    // every tile + this digit in earlier tiles.
+    uint32_t dtot = 0u;
+    if (tid < 256) {
+        uint32_t run = 0u;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const uint32_t c = s_wcnt[w][tid];
+            s_wcnt[w][tid] = run;
+            run += c;
+        }
+        dtot = totals[tid];
+    }
+    uint32_t all;
+    const uint32_t dex = sort_block_scan(tid < 256 ? dtot : 0u, s_warp, all);
+    if (tid < 256) s_dbase[tid] = dex + offsets[(int64_t)tid * ntiles + tile];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kRounds; ++k) {
+        if (val[k] == 0xffffffffu) continue;
+        const uint32_t d = (key[k] >> shift) & 255u;
+        const uint32_t pos = s_dbase[d] + s_wcnt[warp][d] + loc[k];
+        if (pos < (uint64_t)M) {
+            if (!LAST) keys_out[pos] = key[k];
+            vals_out[pos] = val[k];
+        } else {
+            raise_status(status, SPCONV_STATUS_TABLE_FULL);   // inconsistent counts
         }
     }
 }
@@ -988,6 +1209,10 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     uint32_t shift = 32;
     for (int64_t c = L.cap / kGroup; c > 1; c >>= 1) --shift;   // 32 - log2(groups)
     const int MW = spconv_mask_words(V);
+    // Stable radix-sort order for kernels of <= kSortMaxV offsets when the workspace has room
+    // (M >= kSortMinVoxels); the map kernels then skip the bucket histogram.
+    const bool radix = L.sort_tiles > 0 && V <= kSortMaxV;
+    if (radix) hist = nullptr;
 
     stage_mark(SPCONV_STAGE_MEMSET, 0, stream);
     if (cudaMemsetAsync(workspace, 0, (size_t)L.total, stream) != cudaSuccess)
@@ -1064,12 +1289,36 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     if (int rc = check_launch("map_kernel")) return rc;
     stage_mark(SPCONV_STAGE_MAP, 1, stream);
 
-    const int per_block = kOrderThreads * kOrderPerThread;
-    const int ord_grid = (int)((M + per_block - 1) / per_block);
     stage_mark(SPCONV_STAGE_ORDER, 0, stream);
-    launch_pdl(order_kernel, dim3(ord_grid), dim3(kOrderThreads), 0, stream, (const uint32_t *)masks, M, MW,
-               cursor, order, status);
-    if (int rc = check_launch("order_kernel")) return rc;
+    if (radix) {
+        const int nt = L.sort_tiles, passes = sort_passes(V);
+        uint32_t *counts = (uint32_t *)(ws + L.sort_counts);
+        uint32_t *totals = counts + (int64_t)kSortMaxPasses * 256 * nt;
+        uint32_t *tbl = (uint32_t *)table;                      // 4 x M words
+        uint32_t *kb[2] = {tbl, tbl + 2 * M}, *vb[2] = {tbl + M, tbl + 3 * M};
+        for (int p = 0; p < passes; ++p) {
+            uint32_t *cp = counts + (int64_t)p * 256 * nt, *tp = totals + p * 256;
+            const bool first = p == 0, last = p + 1 == passes;
+            uint32_t *ko = kb[p & 1], *vo = last ? (uint32_t *)order : vb[p & 1];
+            const uint32_t *ki = first ? nullptr : kb[(p + 1) & 1], *vi = first ? nullptr : vb[(p + 1) & 1];
+            launch_pdl(first ? sort_count_kernel<true> : sort_count_kernel<false>, dim3(nt), dim3(kSortThreads),
+                       0, stream, (const uint32_t *)masks, V, ki, M, nt, 8 * p, cp);
+            if (int rc = check_launch("sort_count_kernel")) return rc;
+            launch_pdl(sort_scan_kernel, dim3(256), dim3(kSortThreads), 0, stream, cp, nt, tp);
+            if (int rc = check_launch("sort_scan_kernel")) return rc;
+            auto fn = first ? (last ? sort_scatter_kernel<true, true> : sort_scatter_kernel<true, false>)
+                            : (last ? sort_scatter_kernel<false, true> : sort_scatter_kernel<false, false>);
+            launch_pdl(fn, dim3(nt), dim3(kSortThreads), 0, stream, (const uint32_t *)masks, V, ki, vi, M, nt,
+                       8 * p, (const uint32_t *)cp, (const uint32_t *)tp, ko, vo, status);
+            if (int rc = check_launch("sort_scatter_kernel")) return rc;
+        }
+    } else {
+        const int per_block = kOrderThreads * kOrderPerThread;
+        const int ord_grid = (int)((M + per_block - 1) / per_block);
+        launch_pdl(order_kernel, dim3(ord_grid), dim3(kOrderThreads), 0, stream, (const uint32_t *)masks, M, MW,
+                   cursor, order, status);
+        if (int rc = check_launch("order_kernel")) return rc;
+    }
     stage_mark(SPCONV_STAGE_ORDER, 1, stream);
     return SPCONV_OK;
 }

@@ -34,6 +34,25 @@ def check_masks_and_order(nbr, masks, order):
     if M:
         cls = np.minimum(valid.sum(1) - 1, 15)[order]
         assert np.all(np.diff(cls) >= 0), "order groups voxels by neighbour-count class"
+    if M >= RADIX_MIN_VOXELS and V <= RADIX_MAX_V:
+        # large maps of small kernels: exactly the stable sort by (class, mask without centre)
+        np.testing.assert_array_equal(order, np.argsort(order_keys(masks[:, 0], V), kind="stable"))
+
+
+RADIX_MIN_VOXELS, RADIX_MAX_V = 1 << 19, 27
+
+
+def order_keys(m, V):
+    """min(popcount - 1, 15) above the top 20 bits of the mask without its centre bit."""
+    m = m.astype(np.int64) & ((1 << V) - 1)
+    c = V // 2
+    comp = (m & ((1 << c) - 1)) | ((m >> (c + 1)) << c)
+    drop = max(V - 1 - 20, 0)
+    popc = np.zeros_like(m)
+    for v in range(V):
+        popc += (m >> v) & 1
+    cls = np.clip(popc - 1, 0, 15)
+    return (cls << (V - 1 - drop)) | (comp >> drop)
 
 
 @pytest.mark.parametrize("name", sorted(gpu_cases.small_cases()))
@@ -136,3 +155,15 @@ def test_hash_only_path_matches_bitmap_path(name):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     np.testing.assert_array_equal(nbr.cpu().numpy().view(np.uint32), oracle.neighbor_map(coords, shape, ks, dil))
+
+
+@pytest.mark.parametrize("ks,dil", [((3, 3, 3), (1, 1, 1)), ((2, 2, 2), (1, 1, 1)), ((3, 3, 1), (1, 1, 1)),
+                                    ((1, 1, 1), (1, 1, 1)), ((3, 3, 3), (2, 2, 2)), ((5, 5, 1), (1, 1, 1))])
+def test_radix_order_large_maps(ks, dil):
+    """Maps of >= 2^19 voxels take the radix-sort order (1 to 4 digit passes by kernel size)."""
+    rng = np.random.default_rng(11)
+    B, R = 1, 128
+    coords = np.ascontiguousarray(np.argwhere(rng.random((B, R, R, R)) < 0.3).astype(np.int32))
+    assert coords.shape[0] >= RADIX_MIN_VOXELS
+    nbr, masks, order = gpu_map(coords, (B, 1, R, R, R), ks, dil)
+    check_masks_and_order(nbr, masks, order)
