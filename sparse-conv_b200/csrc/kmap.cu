@@ -6,21 +6,23 @@
 // (neighbor_map.cu:132-177) that writes only the found entries.
 //
 // Here:
-//   1. one cudaMemsetAsync clears the workspace (table, histogram, counters);
-//   2. insert_kernel: one thread per voxel, a coalesced int4 load, a bounded linear probe
-//      into a power-of-two table of packed 64-bit slots ((key << 32) | row, stored
-//      complemented so that all-zero means empty). Capacity >= 2M keeps the load <= 0.5 and
-//      the table L2-resident (32 MB at 2M voxels);
-//   3. map_kernel: one warp per voxel probes all V offsets (lane l takes offsets l, l+32, ..)
-//      and writes the voxel's V entries as one contiguous store (no pre-fill pass); a ballot
-//      gives each 32-bit word of the voxel's offset mask. A block owns 512 consecutive
-//      voxels, histograms them by an order key (popcount class, mask hash), and the last
-//      block to finish turns the histogram into bucket offsets;
-//   4. order_kernel: a counting-sort scatter of voxel ids by that key, aggregated per block
-//      so the hot bucket takes one global atomic per block.
+//   1. one cudaMemsetAsync clears the workspace (table, bitmap, histogram, cursors);
+//   2. insert_kernel: one thread per voxel, a coalesced int4 load, a CAS into the first free
+//      slot of its 32-byte group of a power-of-two table of packed 64-bit slots
+//      ((key << 32) | row, stored complemented so that all-zero means empty), and the
+//      voxel's bit in an occupancy bitmap of the grid (grids of <= 2^30 cells);
+//   3. a map kernel (map_kernel_k3 for 3x3x3, map_kernel_cols / map_kernel_bm for other
+//      shapes with a bitmap, map_kernel otherwise): one thread per voxel screens its
+//      offsets against the bitmap, probes the table only for occupied cells, stages the
+//      voxel's map row in shared memory (written out coalesced) and builds its offset mask;
+//      each block adds its voxels' order keys (popcount class, mask hash) to a histogram;
+//   4. order: order_kernel scans the histogram in every block and scatters voxel ids by key
+//      (block-aggregated cursor atomics) - or, for maps of >= 2^19 voxels of kernels of
+//      <= 27 offsets, a stable radix sort by (class, mask) (sort_*_kernel).
 // The map is a pure function of the coordinates: for duplicate-free inputs any correct
-// table gives the reference's map bit for bit. The row order used by the conv kernels
-// (`order`) depends on atomics and is unspecified within a bucket; the conv results do not.
+// table gives the reference's map bit for bit. The bucket order (`order`) depends on
+// atomics and is unspecified within a bucket; the radix order is deterministic; the conv
+// results depend on neither.
 #include <cstdio>
 #include <cstdarg>
 #include <cstring>
@@ -32,7 +34,7 @@ namespace spconv {
 
 constexpr int kOrderBuckets = 4096;    // 16 popcount classes x 256 mask-hash buckets
 constexpr int kMapThreads = 128;      // one thread per voxel
-constexpr int kOrderThreads = 256;
+constexpr int kOrderThreads = 256;      // kOrderBuckets / kOrderThreads must be a multiple of 4
 constexpr int kOrderPerThread = 2;     // voxels per thread in order_kernel
 // Radix-sort order (kernels of at most kSortMaxV offsets, at least kSortMinVoxels voxels):
 // tiles of kSortTile voxels, 8-bit digits, keys of at most 31 bits.
@@ -65,7 +67,7 @@ struct WsLayout {
     int64_t cap = 0;
     bool key64 = false;
     int64_t bitmap_words = 0;
-    int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, counter = 0, total = 0;
+    int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, total = 0;
     int sort_tiles = 0;            // > 0: room for the radix-sort order (keys alias the table)
     int64_t sort_counts = 0;       // [kSortMaxPasses][256][sort_tiles] + [kSortMaxPasses][256] totals
 };
@@ -97,7 +99,6 @@ static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
     if (L.bitmap_words) { L.bitmap = off; off += align256(L.bitmap_words * 4); }
     L.hist = off; off += align256(kOrderBuckets * 4);
     L.cursor = off; off += align256(kOrderBuckets * 4);
-    L.counter = off; off += 256;
     if (M >= kSortMinVoxels) {
         // Sort keys and values (4 x M words) reuse the table, dead once the map is built:
         // its capacity is at least 2M slots of 8 bytes.
@@ -107,6 +108,14 @@ static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
     }
     L.total = off;
     return L;
+}
+
+// Adds a block's shared-memory order histogram to the global one (after a __syncthreads).
+// The order kernel turns the global histogram into bucket offsets; nothing here waits on
+// other blocks.
+__device__ __forceinline__ void block_hist_flush(const uint32_t *s_hist, uint32_t *hist) {
+    for (int b = threadIdx.x; b < kOrderBuckets; b += blockDim.x)
+        if (s_hist[b]) atomicAdd(hist + b, s_hist[b]);
 }
 
 // Warp-aggregated shared-memory increment: returns this lane's rank among all increments
@@ -247,10 +256,8 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
            int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
            const unsigned long long *__restrict__ table, const uint32_t *__restrict__ vals,
            const uint32_t *__restrict__ bitmap, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr, uint32_t *__restrict__ masks,
-           uint32_t *hist, uint32_t *cursor, uint32_t *done_counter, int32_t *status) {
+           uint32_t *hist, int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
-    __shared__ uint32_t s_is_last;
-    __shared__ uint32_t s_warp[kMapThreads / 32];
     extern __shared__ int4 s_off[];                                   // [V] (ox, oy, oz, 0)
     long long *s_delta = reinterpret_cast<long long *>(s_off + V);   // [V] flat-key deltas
     int32_t *s_stage = reinterpret_cast<int32_t *>(s_delta + V);     // [kMapThreads][vstride]
@@ -357,34 +364,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             if (v >= V) { v -= V; ++il; }
         }
     }
-    if (hist == nullptr) return;                                // radix-sort order: no histogram
-    for (int b = tid; b < kOrderBuckets; b += kMapThreads)
-        if (s_hist[b]) atomicAdd(hist + b, s_hist[b]);
-
-    // The last block to finish converts the global histogram into bucket start offsets.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_is_last = (atomicAdd(done_counter, 1u) == gridDim.x - 1) ? 1u : 0u;
-    __syncthreads();
-    if (!s_is_last) return;
-    __threadfence();
-    constexpr int per = kOrderBuckets / kMapThreads;
-    uint32_t local[per];
-    uint32_t sum = 0;
-#pragma unroll
-    for (int k = 0; k < per; ++k) { local[k] = __ldcg(hist + tid * per + k); sum += local[k]; }
-    uint32_t incl = sum;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += n;
-    }
-    if (lane == 31) s_warp[warp] = incl;
-    __syncthreads();
-    uint32_t run = incl - sum;
-    for (int w = 0; w < warp; ++w) run += s_warp[w];
-#pragma unroll
-    for (int k = 0; k < per; ++k) { cursor[tid * per + k] = run; run += local[k]; }
+    if (hist) block_hist_flush(s_hist, hist);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -398,50 +378,15 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
 constexpr int kMapBmMaxThreads = 256;
 constexpr int kColBatchMax = 8;          // Kd <= 8 (longer columns use map_kernel)
 
-__device__ __forceinline__ void block_hist_flush_and_scan(uint32_t *s_hist, uint32_t *s_warp,
-                                                          uint32_t *s_is_last, uint32_t *hist,
-                                                          uint32_t *cursor, uint32_t *done_counter) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
-    for (int b = tid; b < kOrderBuckets; b += nthr)
-        if (s_hist[b]) atomicAdd(hist + b, s_hist[b]);
-    // The last block to finish converts the global histogram into bucket start offsets.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *s_is_last = (atomicAdd(done_counter, 1u) == gridDim.x - 1) ? 1u : 0u;
-    __syncthreads();
-    if (!*s_is_last) return;
-    __threadfence();
-    const int per = kOrderBuckets / nthr;             // 16 (256 threads) or 32 (128 threads)
-    uint32_t sum = 0;
-    for (int k = 0; k < per; ++k) sum += __ldcg(hist + tid * per + k);
-    uint32_t incl = sum;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += n;
-    }
-    if (lane == 31) s_warp[warp] = incl;
-    __syncthreads();
-    uint32_t run = incl - sum;
-    for (int w = 0; w < warp; ++w) run += s_warp[w];
-    for (int k = 0; k < per; ++k) {
-        const uint32_t c = __ldcg(hist + tid * per + k);
-        cursor[tid * per + k] = run;
-        run += c;
-    }
-}
-
 template <int kColBatch>
 __global__ void __launch_bounds__(kMapBmMaxThreads, 3)
 map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
               int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
-              uint32_t *__restrict__ masks, uint32_t *hist, uint32_t *cursor, uint32_t *done_counter,
+              uint32_t *__restrict__ masks, uint32_t *hist,
               int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
-    __shared__ uint32_t s_is_last;
-    __shared__ uint32_t s_warp[kMapBmMaxThreads / 32];
     extern __shared__ int32_t s_stage[];                       // [blockDim.x][vstride]
 
     const int tid = threadIdx.x, nthr = blockDim.x;
@@ -563,7 +508,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             }
         }
     }
-    if (hist) block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+    if (hist) block_hist_flush(s_hist, hist);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -582,12 +527,10 @@ __global__ void __launch_bounds__(kMapK3Threads, 3)
 map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
-              uint32_t *__restrict__ masks, uint32_t *hist, uint32_t *cursor, uint32_t *done_counter,
+              uint32_t *__restrict__ masks, uint32_t *hist,
               int32_t *status) {
     constexpr int V = 27;
     __shared__ uint32_t s_hist[kOrderBuckets];
-    __shared__ uint32_t s_is_last;
-    __shared__ uint32_t s_warp[kMapK3Threads / 32];
     __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
 
     const int tid = threadIdx.x;
@@ -717,7 +660,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
         for (int e = tid; e < n4; e += kMapK3Threads) dst[e] = src[e];
         for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
     }
-    if (hist) block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+    if (hist) block_hist_flush(s_hist, hist);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -756,11 +699,8 @@ __global__ void __launch_bounds__(kMapColsThreads)
 map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Kw, int Kh, int Kd,
                 int Dw, int Dh, int Dd, int V, int MW, const unsigned long long *__restrict__ table,
                 const uint32_t *__restrict__ bitmap, int64_t bm_words, uint64_t gmask, uint32_t shift,
-                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, uint32_t *cursor,
-                uint32_t *done_counter, int32_t *status) {
+                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
-    __shared__ uint32_t s_is_last;
-    __shared__ uint32_t s_warp[kMapColsThreads / 32];
     extern __shared__ int4 s_stage4[];                           // [kMapColsThreads * V] int32, padded to 16 B
     int32_t *s_stage = reinterpret_cast<int32_t *>(s_stage4);
 
@@ -904,22 +844,50 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             for (int e = tid; e < total; e += kMapColsThreads) out[e] = s_stage[e];
         }
     }
-    if (hist) block_hist_flush_and_scan(s_hist, s_warp, &s_is_last, hist, cursor, done_counter);
+    if (hist) block_hist_flush(s_hist, hist);
 }
 
 // ---------------------------------------------------------------------------------------
-// 3. Counting-sort scatter of voxel ids by order key.
+// 3. Counting-sort scatter of voxel ids by order key. Every block scans the map kernel's
+//    global histogram (16 KB from L2) into bucket starts itself, so no block of the map
+//    kernel waits for the others; a bucket's voxels of one block take one cursor atomic.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kOrderThreads)
-order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, uint32_t *cursor,
-             int32_t *__restrict__ order, int32_t *status) {
+order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, const uint32_t *hist,
+             uint32_t *cursor, int32_t *__restrict__ order, int32_t *status) {
+    constexpr int kPer = kOrderBuckets / kOrderThreads;        // 16 buckets per thread
     __shared__ uint32_t s_cnt[kOrderBuckets];
-    __shared__ uint32_t s_base[kOrderBuckets];
-    const int tid = threadIdx.x;
+    __shared__ __align__(16) uint32_t s_base[kOrderBuckets];
+    __shared__ uint32_t s_warp[kOrderThreads / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t i0 = (int64_t)blockIdx.x * (kOrderThreads * kOrderPerThread);
     for (int b = tid; b < kOrderBuckets; b += kOrderThreads) s_cnt[b] = 0u;
-    grid_dependency_wait();                                     // the map kernel's masks and cursors
+    grid_dependency_wait();                                     // the map kernel's masks and histogram
     grid_launch_dependents();
+    {
+        // bucket starts: exclusive scan of the histogram, buckets tid*kPer .. tid*kPer+kPer-1 here
+        uint32_t local[kPer];
+        uint32_t sum = 0;
+        const uint4 *h4 = reinterpret_cast<const uint4 *>(hist + tid * kPer);
+#pragma unroll
+        for (int q = 0; q < kPer / 4; ++q) {
+            const uint4 v = __ldcg(h4 + q);
+            local[4 * q] = v.x; local[4 * q + 1] = v.y; local[4 * q + 2] = v.z; local[4 * q + 3] = v.w;
+            sum += v.x + v.y + v.z + v.w;
+        }
+        uint32_t incl = sum;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t n = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += n;
+        }
+        if (lane == 31) s_warp[warp] = incl;
+        __syncthreads();
+        uint32_t run = incl - sum;
+        for (int w = 0; w < warp; ++w) run += s_warp[w];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) { s_base[tid * kPer + k] = run; run += local[k]; }
+    }
     __syncthreads();
     uint32_t key[kOrderPerThread], rank[kOrderPerThread];
 #pragma unroll
@@ -939,7 +907,7 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, uint32_t *cu
     }
     __syncthreads();
     for (int b = tid; b < kOrderBuckets; b += kOrderThreads)
-        if (s_cnt[b]) s_base[b] = atomicAdd(cursor + b, s_cnt[b]);
+        if (s_cnt[b]) s_base[b] += atomicAdd(cursor + b, s_cnt[b]);
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kOrderPerThread; ++k) {
@@ -1204,7 +1172,6 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     uint32_t *bitmap = L.bitmap_words ? (uint32_t *)(ws + L.bitmap) : nullptr;
     uint32_t *hist = (uint32_t *)(ws + L.hist);
     uint32_t *cursor = (uint32_t *)(ws + L.cursor);
-    uint32_t *counter = (uint32_t *)(ws + L.counter);
     const uint64_t gmask = (uint64_t)(L.cap / kGroup) - 1;
     uint32_t shift = 32;
     for (int64_t c = L.cap / kGroup; c > 1; c >>= 1) --shift;   // 32 - log2(groups)
@@ -1235,7 +1202,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         launch_pdl(k3_fn, dim3(grid), dim3(kMapK3Threads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, (const unsigned long long *)table,
                    (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
-                   cursor, counter, status);
+                   status);
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
         const size_t smem = ((size_t)kMapColsThreads * V * sizeof(int32_t) + 15) / 16 * 16;
         static bool cols_attr_done = false;
@@ -1248,7 +1215,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         launch_pdl(map_kernel_cols, dim3(grid), dim3(kMapColsThreads), smem, stream,
                    (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW,
                    (const unsigned long long *)table, (const uint32_t *)bitmap, L.bitmap_words, gmask,
-                   shift, neighbor_map, masks, hist, cursor, counter, status);
+                   shift, neighbor_map, masks, hist, status);
     } else if (bitmap && Kd <= kColBatchMax) {
         // 256 voxels per block while their staged rows fit in 64 KB, else 128.
         const int nthr = ((size_t)kMapBmMaxThreads * (V | 1) * 4 <= 64 * 1024) ? kMapBmMaxThreads : 128;
@@ -1265,7 +1232,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         bm_fn<<<grid, nthr, smem, stream>>>(
             (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, bitmap,
-            L.bitmap_words, gmask, shift, neighbor_map, masks, hist, cursor, counter, status);
+            L.bitmap_words, gmask, shift, neighbor_map, masks, hist, status);
     } else {
         const int map_grid = (int)((M + kMapThreads - 1) / kMapThreads);
         // Rows are staged in shared memory (odd row stride: conflict-free) unless V is so
@@ -1284,7 +1251,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         map_fn<<<map_grid, kMapThreads, map_smem, stream>>>(
             (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, bitmap,
-            gmask, shift, neighbor_map, masks, hist, cursor, counter, status);
+            gmask, shift, neighbor_map, masks, hist, status);
     }
     if (int rc = check_launch("map_kernel")) return rc;
     stage_mark(SPCONV_STAGE_MAP, 1, stream);
@@ -1316,7 +1283,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         const int per_block = kOrderThreads * kOrderPerThread;
         const int ord_grid = (int)((M + per_block - 1) / per_block);
         launch_pdl(order_kernel, dim3(ord_grid), dim3(kOrderThreads), 0, stream, (const uint32_t *)masks, M, MW,
-                   cursor, order, status);
+                   (const uint32_t *)hist, cursor, order, status);
         if (int rc = check_launch("order_kernel")) return rc;
     }
     stage_mark(SPCONV_STAGE_ORDER, 1, stream);
