@@ -62,7 +62,8 @@ int spconv_abi_version(void);
 const char *spconv_last_error(void);
 
 /* Slots of the coordinate hash table for num_coords voxels: the next power of two
- * >= 2 * num_coords (at least 1024), so the load factor stays in (0.25, 0.5].
+ * >= 4 * num_coords while that table stays <= 64 MB (load <= 0.25), else the next power of
+ * two >= 2 * num_coords (load <= 0.5); at least 1024.
  * Replaces the sizing of ops/utils.py:3-16 + ops/submanifold_conv3d.py:43-45. */
 int64_t spconv_hashmap_capacity(int64_t num_coords);
 
@@ -84,9 +85,12 @@ int64_t spconv_neighbor_map_workspace_bytes(int64_t num_coords, int batch, int W
  *                entry v == V/2 is the voxel's own row. Bit-identical to the reference's
  *                uint32 map (neighbor_map.cu:145-176).
  *   masks        [M, spconv_mask_words(V)] uint32 output: bit v set iff neighbor_map[i,v] >= 0
- *   order        [M] int32 output: a permutation of 0..M-1 that groups voxels with equal
- *                popcount and similar masks (the conv kernels' tile order). Its order within
- *                a group is unspecified; conv results do not depend on it.
+ *   order        [M] int32 output: a permutation of 0..M-1, the conv kernels' tile order.
+ *                For M >= 2^19 and V <= 27 it is the stable sort of the voxels by
+ *                key = min(popcount(mask) - 1, 15) << b | (mask without bit V/2) >> d, where
+ *                d = max(V - 21, 0) and b = V - 1 - d (deterministic). Otherwise it groups
+ *                voxels by that class and a hash of the mask, in an unspecified order inside
+ *                a group. Conv results do not depend on it.
  *   status       device int32, OR-ed with SPCONV_STATUS_* bits
  * Replaces neighbor_map.h:16-28 (hashmap_build_submanifold_conv_neighbor_map_cuda_naive). */
 int spconv_build_submanifold_neighbor_map(
