@@ -157,6 +157,30 @@ int spconv_submanifold_conv_forward_ex(
     const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
     void *out, int32_t *status, void *stream, int kernel_choice);
 
+/* Transposed kernel map for the input gradient: neighbor_map_t[j, v] = i where
+ * neighbor_map[i, v] = j (at most one such i for distinct coordinates; the largest if the
+ * coordinates repeat), -1 if none; masks_t (optional, [M, spconv_mask_words(V)]) its offset
+ * masks. For odd kernel sizes this equals the reference's flipped map
+ * torch.flip(neighbor_map, [1]) (ops/submanifold_conv3d.py:123-126); for even sizes it is
+ * the exact transpose (the flip is not, as the offsets are not symmetric).
+ * The input gradient is then spconv_submanifold_conv_forward(grad_out, ..., weight_t, NULL,
+ * ..., neighbor_map_t, masks_t, order) with weight_t[ci, v, co] = weight[co, v, ci]. */
+int spconv_transpose_neighbor_map(
+    const int32_t *neighbor_map, int64_t num_coords, int kernel_volume,
+    int32_t *neighbor_map_t, uint32_t *masks_t, int32_t *status, void *stream);
+
+/* Weight and bias gradients of the submanifold conv (fp32, overwritten):
+ *   grad_weight[co, v, ci] = sum_i grad_out[i, co] * feats[neighbor_map[i, v], ci]
+ *   grad_bias[co]          = sum_i grad_out[i, co]           (grad_bias may be NULL)
+ * feats [M, Ci] and grad_out [M, Co] in dtype; order (optional) = the map build's order,
+ * used to skip 128-voxel tiles without a neighbour at an offset. Accumulates with fp32
+ * atomics, so the last bits may differ from run to run.
+ * Replaces the EXPLICIT_GEMM weight / bias gradient of ops/submanifold_conv3d.py:132-143. */
+int spconv_submanifold_conv_weight_grad(
+    const void *feats, const void *grad_out, int dtype, int64_t num_coords, int Ci, int Co,
+    int kernel_volume, const int32_t *neighbor_map, const int32_t *order,
+    float *grad_weight, float *grad_bias, int32_t *status, void *stream);
+
 /* Stage timing, for profiling and for the benchmark's roofline figures.
  * spconv_stage_timing(max_calls > 0) creates CUDA events on the current device for
  * max_calls calls of each stage and starts recording, on the launch stream, the device

@@ -51,6 +51,11 @@ SIGNATURES = {
         _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_transpose_neighbor_map": (_c_int, [
+        _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_submanifold_conv_weight_grad": (_c_int, [
+        _c_void_p, _c_void_p, _c_int, _c_i64, _c_int, _c_int, _c_int,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_stage_timing": (_c_int, [_c_int]),
     "spconv_stage_times_ms": (_c_int, [_c_void_p, _c_void_p, _c_int]),
 }
@@ -315,6 +320,62 @@ def conv_forward(feats: torch.Tensor, weight: torch.Tensor, bias: Optional[torch
     if rc != SPCONV_OK:
         _raise(rc, "spconv_submanifold_conv_forward")
     return out
+
+
+def transpose_neighbor_map(nbr: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(nbr_t, masks_t): nbr_t[j, v] = i where nbr[i, v] = j (-1 if none), and its offset masks."""
+    lib = load_library()
+    dev = _require_cuda(nbr)
+    nb = nbr.view(torch.int32) if nbr.dtype == torch.uint32 else nbr
+    if nb.dtype != torch.int32 or nb.dim() != 2 or not nb.is_contiguous():
+        raise ValueError("neighbor map must be a contiguous [M, V] int32/uint32 tensor")
+    M, V = int(nb.shape[0]), int(nb.shape[1])
+    nbr_t = torch.empty((M, V), dtype=torch.int32, device=dev)
+    masks_t = torch.empty((M, mask_words(V)), dtype=torch.int32, device=dev)
+    if M == 0:
+        return nbr_t, masks_t
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_transpose_neighbor_map(nb.data_ptr(), M, V, nbr_t.data_ptr(), masks_t.data_ptr(),
+                                           st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_transpose_neighbor_map")
+    return nbr_t, masks_t
+
+
+def conv_weight_grad(feats: torch.Tensor, grad_out: torch.Tensor, nbr: torch.Tensor,
+                     order: Optional[torch.Tensor], with_bias: bool = True
+                     ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """(grad_weight [Co, V, Ci] fp32, grad_bias [Co] fp32 or None) of the submanifold conv:
+    grad_weight[co, v, ci] = sum_i grad_out[i, co] * feats[nbr[i, v], ci]."""
+    lib = load_library()
+    dev = _require_cuda(feats, grad_out, nbr, order)
+    if feats.dtype not in DTYPE_CODES:
+        raise TypeError(f"unsupported feature dtype {feats.dtype}")
+    if grad_out.dtype != feats.dtype:
+        raise TypeError(f"grad_out dtype {grad_out.dtype} differs from feats dtype {feats.dtype}")
+    if not (feats.is_contiguous() and grad_out.is_contiguous()):
+        raise ValueError("feats and grad_out must be contiguous")
+    nb = nbr.view(torch.int32) if nbr.dtype == torch.uint32 else nbr
+    if nb.dtype != torch.int32 or nb.dim() != 2 or not nb.is_contiguous():
+        raise ValueError("neighbor map must be a contiguous [M, V] int32/uint32 tensor")
+    M, Ci = int(feats.shape[0]), int(feats.shape[1])
+    Co, V = int(grad_out.shape[1]), int(nb.shape[1])
+    if grad_out.shape[0] != M or nb.shape[0] != M:
+        raise ValueError("feats, grad_out and neighbor map must have the same number of rows")
+    if order is not None and (order.dtype != torch.int32 or order.numel() != M or not order.is_contiguous()):
+        raise ValueError("order must be a contiguous [M] int32 tensor")
+    gw = torch.empty((Co, V, Ci), dtype=torch.float32, device=dev)
+    gb = torch.empty((Co,), dtype=torch.float32, device=dev) if with_bias else None
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_submanifold_conv_weight_grad(
+        feats.data_ptr(), grad_out.data_ptr(), DTYPE_CODES[feats.dtype], M, Ci, Co, V, nb.data_ptr(),
+        None if order is None else order.data_ptr(), gw.data_ptr(),
+        None if gb is None else gb.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_submanifold_conv_weight_grad")
+    return gw, gb
 
 
 def stage_timing(max_calls: int) -> None:

@@ -23,6 +23,9 @@ Differences, all deliberate:
 * Bias is added in fp32 before the single rounding to the feature dtype (the reference's
   Triton kernel rounds first and adds the bias in the feature dtype).
 * Out-of-range coordinates raise ``RuntimeError`` (the reference silently aliases keys).
+* The backward runs (the reference's autograd ``backward`` cannot be called, ``ops:186-206``):
+  the input gradient uses the exact transposed map, which for even kernel sizes differs from
+  the reference's flipped map (``ops:123-126``); for odd sizes they are the same.
 """
 from __future__ import annotations
 
@@ -84,8 +87,8 @@ class SubMConv3dFunction(Function):
     ) -> SubMConv3dNeighborCache:
         """Build the kernel map of ``coords`` (ops:29-61).
 
-        ``hashmap_ratio`` is accepted for signature compatibility; the table always has
-        the next power of two >= 2M slots (load factor <= 0.5), which the library sizes.
+        ``hashmap_ratio`` is accepted for signature compatibility; the library sizes the
+        table itself (the next power of two >= 4M slots while that stays <= 64 MB, else >= 2M).
         """
         assert coords.is_contiguous(), "Coords should be contiguous."
         assert coords.dtype == torch.int32, "Unsupported coords dtype. Expected int32."
@@ -126,6 +129,54 @@ class SubMConv3dFunction(Function):
         return out
 
     @staticmethod
+    def _sparse_submanifold_conv_backward(
+        grad_output: torch.Tensor,
+        feats: torch.Tensor,
+        neighbor_cache: SubMConv3dNeighborCache,
+        weight: torch.Tensor,
+        bias: Optional[torch.Tensor] = None,
+        algorithm: str = Algorithm.EXPLICIT_GEMM,
+        needs: Tuple[bool, bool, bool] = None,
+    ) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor], Optional[torch.Tensor]]:
+        """(grad_feats, grad_weight, grad_bias) of the conv (ops:105-150); every algorithm runs
+        the CUDA kernels.
+
+        grad_feats is a forward conv of grad_output over the transposed map (cached on
+        ``neighbor_cache`` as ``neighbor_map_t`` / ``masks_t``) with the weight's channel axes
+        swapped. For odd kernel sizes the transposed map is the reference's flipped map
+        (ops:123-126); for even sizes it is the exact transpose, where the flip is not.
+        grad_weight / grad_bias are accumulated in fp32 and returned in the parameters' dtypes.
+        ``needs`` = which of (feats, weight, bias) want a gradient (default: requires_grad).
+        """
+        if algorithm not in _ALGORITHMS:
+            raise ValueError(f"Unsupported Algorithm {algorithm}.")
+        if needs is None:
+            needs = (feats.requires_grad, weight.requires_grad,
+                     bias is not None and bias.requires_grad)
+        Co, Kw, Kh, Kd, Ci = weight.shape
+        V = Kw * Kh * Kd
+        nbr, _masks, order = _cache_tensors(neighbor_cache)
+        g = grad_output.to(feats.dtype).contiguous()
+        grad_input = grad_weight = grad_bias = None
+        if needs[0]:
+            nbr_t = getattr(neighbor_cache, "neighbor_map_t", None)
+            masks_t = getattr(neighbor_cache, "masks_t", None)
+            if nbr_t is None:
+                nbr_t, masks_t = _native.transpose_neighbor_map(nbr)
+                neighbor_cache.neighbor_map_t, neighbor_cache.masks_t = nbr_t, masks_t
+            w_t = weight.reshape(Co, V, Ci).permute(2, 1, 0).to(feats.dtype).contiguous()
+            grad_input = _native.conv_forward(g, w_t, None, nbr_t, masks_t, order)
+        if needs[1] or (bias is not None and needs[2]):
+            gw, gb = _native.conv_weight_grad(feats.contiguous(), g, nbr, order,
+                                              with_bias=bias is not None and needs[2])
+            if needs[1]:
+                grad_weight = gw.view(Co, Kw, Kh, Kd, Ci).to(weight.dtype)
+            if gb is not None:
+                grad_bias = gb.to(bias.dtype)
+        _native.after_launch(g.device)
+        return grad_input, grad_weight, grad_bias
+
+    @staticmethod
     def forward(
         ctx,
         feats: torch.Tensor,
@@ -147,13 +198,19 @@ class SubMConv3dFunction(Function):
             feats, neighbor_cache, weight, bias, algorithm)
         ctx.save_for_backward(feats, weight, bias)
         ctx.neighbor_cache = neighbor_cache
+        ctx.algorithm = algorithm
         return output, neighbor_cache
 
     @staticmethod
     def backward(ctx, grad_output: torch.Tensor, _grad_cache=None):
-        raise NotImplementedError(
-            "sparseconv: the submanifold conv backward is not available in this build "
-            "(the reference's backward is not functional either)")
+        """Gradients for feats, weight and bias (ops:186-206, whose signature there cannot
+        be called by autograd: it takes the cache's gradient as the algorithm)."""
+        feats, weight, bias = ctx.saved_tensors
+        needs = (ctx.needs_input_grad[0], ctx.needs_input_grad[4],
+                 bias is not None and ctx.needs_input_grad[5])
+        grad_input, grad_weight, grad_bias = SubMConv3dFunction._sparse_submanifold_conv_backward(
+            grad_output, feats, ctx.neighbor_cache, weight, bias, ctx.algorithm, needs)
+        return grad_input, None, None, None, grad_weight, grad_bias, None, None
 
 
 def sparse_submanifold_conv3d(
