@@ -169,17 +169,24 @@ int spconv_transpose_neighbor_map(
     const int32_t *neighbor_map, int64_t num_coords, int kernel_volume,
     int32_t *neighbor_map_t, uint32_t *masks_t, int32_t *status, void *stream);
 
+/* Bytes of workspace spconv_submanifold_conv_weight_grad uses for num_coords voxels (tile
+ * offset unions and per-offset-group tile lists), or -1 for invalid arguments. */
+int64_t spconv_weight_grad_workspace_bytes(int64_t num_coords, int kernel_volume);
+
 /* Weight and bias gradients of the submanifold conv (fp32, overwritten):
  *   grad_weight[co, v, ci] = sum_i grad_out[i, co] * feats[neighbor_map[i, v], ci]
  *   grad_bias[co]          = sum_i grad_out[i, co]           (grad_bias may be NULL)
- * feats [M, Ci] and grad_out [M, Co] in dtype; order (optional) = the map build's order,
- * used to skip 128-voxel tiles without a neighbour at an offset. Accumulates with fp32
- * atomics, so the last bits may differ from run to run.
+ * feats [M, Ci] and grad_out [M, Co] in dtype; masks / order (optional) from the map build.
+ * 16-bit features with 16/32/64/128 channels run on the tensor cores when a 16-byte aligned
+ * workspace of spconv_weight_grad_workspace_bytes() is given: 128-voxel tiles of the order
+ * that have no neighbour at an offset are skipped. Other cases run on the CUDA cores.
+ * Accumulates with fp32 atomics, so the last bits may differ from run to run.
  * Replaces the EXPLICIT_GEMM weight / bias gradient of ops/submanifold_conv3d.py:132-143. */
 int spconv_submanifold_conv_weight_grad(
     const void *feats, const void *grad_out, int dtype, int64_t num_coords, int Ci, int Co,
-    int kernel_volume, const int32_t *neighbor_map, const int32_t *order,
-    float *grad_weight, float *grad_bias, int32_t *status, void *stream);
+    int kernel_volume, const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
+    float *grad_weight, float *grad_bias, void *workspace, int64_t workspace_bytes,
+    int32_t *status, void *stream);
 
 /* Stage timing, for profiling and for the benchmark's roofline figures.
  * spconv_stage_timing(max_calls > 0) creates CUDA events on the current device for

@@ -12,12 +12,13 @@
 // sizes the flip is not the transpose (offsets are not symmetric) and this is the exact one.
 //
 // The weight gradient is a reduction over voxels per offset. wgrad_mma_kernel (16-bit
-// features, 64 or 128 channels on both sides): one CTA per (offset, run of tiles of the voxel
-// order), 128 voxels per tile gathered by cp.async into padded shared-memory rows in the
-// order they sit in HBM (voxel-major), and read by ldmatrix.trans straight into mma.sync
-// fragments (A = grad_out^T, B = feats^T, K = voxels); tiles whose 128 voxels have no
-// neighbour at that offset are skipped. Fp32 accumulators are added to the fp32 gradient
-// once per CTA. wgrad_simt_kernel covers the other dtypes and channel counts.
+// features, 16/32/64/128 channels on both sides): one CTA per (group of offsets, run of tiles
+// of the voxel order); per 128-voxel tile the grad_out rows are gathered once for the group
+// and each offset's neighbour feature rows beside them, by cp.async into padded shared-memory
+// rows in the order they sit in HBM (voxel-major), read by ldmatrix.trans straight into
+// mma.sync fragments (A = grad_out^T, B = feats^T, K = voxels). Tiles whose voxels have no
+// neighbour at any of the group's offsets are skipped. Fp32 accumulators are added to the
+// fp32 gradient once per CTA. wgrad_simt_kernel covers fp32 and other channel counts.
 #include <type_traits>
 
 #include "common.cuh"
@@ -86,97 +87,265 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t add
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
 }
 
-// CO / 16 warps; warp w owns output rows 16w..16w+15 (co) and every column (ci).
+// Offsets per group: the grad_out tile is gathered once for OG offsets; warp w owns offset
+// w / (CO/16) of the group and output rows 16 (w % (CO/16)) .. +15 (all CI columns), so a CTA
+// has OG * CO / 16 warps (<= 16). Two pipeline stages of (grad_out tile + OG feature tiles)
+// fit in ~220 KB of shared memory; shapes left with fewer than four warps run on the CUDA cores.
 template <typename T, int CO, int CI>
-__global__ void __launch_bounds__(CO * 2)
+struct WgCfg {
+    static constexpr int GP = CO + 8, FP = CI + 8;        // padded row pitch (elements): conflict-free ldmatrix
+    static constexpr int kGBytes = kWgTile * GP * 2;
+    static constexpr int kFBytes = kWgTile * FP * 2;
+    static constexpr int kOgWarps = (CI >= 128 ? 128 : 256) / CO;   // 16 warps (8 with 64 accumulators a thread)
+    // small rows: ~55 KB a stage (two CTAs per SM hide the index latency); else ~110 KB
+    static constexpr int kStageBudget = (CO <= 32 && CI <= 32 ? 55 : 110) * 1024;
+    static constexpr int kOgSmem = (kStageBudget - kGBytes - 4 * kWgTile) / (kFBytes + 4 * kWgTile);
+    static constexpr int OG = kOgWarps < kOgSmem ? kOgWarps : kOgSmem;
+    static constexpr int kWarps = OG * CO / 16;
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kStageBytes = kGBytes + OG * kFBytes + kWgTile * 4 * (1 + OG);
+    static constexpr int kSmem = 2 * kStageBytes + 1024 * 4;             // + group counts
+    static constexpr bool kSupported = kWarps >= 4;
+};
+
+constexpr int kWgMaxGroups = 1024;
+
+// Offset masks OR-ed over each 128-voxel tile of the voxel order: union[t][w], MW words.
+__global__ void __launch_bounds__(kWgTile)
+tile_union_kernel(const uint32_t *__restrict__ masks, const int32_t *__restrict__ nbr,
+                  const int32_t *__restrict__ order, int64_t M, int V, int MW, uint32_t *__restrict__ uni) {
+    __shared__ uint32_t s_or[kWgTile / 32][32];
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t p = (int64_t)t * kWgTile + tid;
+    int32_t row = -1;
+    if (p < M) {
+        row = order ? __ldg(order + p) : (int32_t)p;
+        if ((uint32_t)row >= (uint32_t)M) row = -1;
+    }
+    for (int w = 0; w < MW; ++w) {
+        uint32_t m = 0;
+        if (row >= 0) {
+            if (masks) {
+                m = __ldg(masks + (int64_t)row * MW + w);
+            } else {
+                const int v1 = min(V, 32 * w + 32);
+                for (int v = 32 * w; v < v1; ++v)
+                    if ((uint32_t)__ldg(nbr + (int64_t)row * V + v) < (uint32_t)M) m |= 1u << (v & 31);
+            }
+        }
+        m = __reduce_or_sync(0xffffffffu, m);
+        if (lane == 0) s_or[warp][w & 31] = m;
+        __syncthreads();
+        if (tid == 0) uni[(int64_t)t * MW + w] = s_or[0][w & 31] | s_or[1][w & 31] | s_or[2][w & 31] | s_or[3][w & 31];
+        __syncthreads();
+    }
+}
+
+// One block per offset group: the tiles with a neighbour at any of the group's offsets, in
+// tile order, as list[g][0 .. cnt[g]).
+__global__ void __launch_bounds__(512)
+group_tiles_kernel(const uint32_t *__restrict__ uni, int num_tiles, int MW, int V, int OG,
+                   int32_t *__restrict__ list, int32_t *__restrict__ cnt) {
+    __shared__ uint32_t s_warp[16];
+    const int g = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lo = g * OG, hi = min(V, lo + OG);
+    int base = 0;
+    for (int t0 = 0; t0 < num_tiles; t0 += 512) {
+        const int t = t0 + tid;
+        bool act = false;
+        if (t < num_tiles) {
+            for (int v = lo; v < hi; ++v)
+                if ((__ldg(uni + (int64_t)t * MW + (v >> 5)) >> (v & 31)) & 1u) { act = true; break; }
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, act);
+        if (lane == 0) s_warp[warp] = __popc(bal);
+        __syncthreads();
+        int off = 0, tot = 0;
+        for (int w = 0; w < 16; ++w) { const int c = s_warp[w]; off += w < warp ? c : 0; tot += c; }
+        if (act) list[(int64_t)g * num_tiles + base + off + __popc(bal & ((1u << lane) - 1u))] = t;
+        base += tot;
+        __syncthreads();
+    }
+    if (tid == 0) cnt[g] = base;
+}
+
+template <typename T, int CO, int CI>
+__global__ void __launch_bounds__(WgCfg<T, CO, CI>::kThreads)
 wgrad_mma_kernel(const T *__restrict__ feats, const T *__restrict__ gout,
                  const int32_t *__restrict__ nbr, const int32_t *__restrict__ order,
-                 int64_t M, int V, int num_tiles, int tiles_per_cta, float *__restrict__ gw) {
-    constexpr int kThreads = CO * 2, kWarps = CO / 16;
-    constexpr int GP = CO + 8, FP = CI + 8;               // padded row pitch (elements): conflict-free ldmatrix
+                 const int32_t *__restrict__ list, const int32_t *__restrict__ cnt,
+                 const uint32_t *__restrict__ uni, int MW,
+                 int64_t M, int V, int num_tiles, int groups, float *__restrict__ gw) {
+    using Cfg = WgCfg<T, CO, CI>;
+    static_assert(Cfg::kSupported && Cfg::kThreads >= kWgTile && Cfg::kThreads <= 512, "thread count");
+    constexpr int OG = Cfg::OG, NT = Cfg::kThreads, GP = Cfg::GP, FP = Cfg::FP;
     constexpr int kNT = CI / 8;                           // n8 tiles per warp
+    constexpr int kMB = CO / 16;                          // m16 blocks per offset
     extern __shared__ __align__(16) uint8_t wg_smem[];
-    T *Gs = reinterpret_cast<T *>(wg_smem);               // [kWgTile][GP]
-    T *Fs = Gs + kWgTile * GP;                            // [kWgTile][FP]
+    int32_t *s_cnt = reinterpret_cast<int32_t *>(wg_smem + 2 * Cfg::kStageBytes);   // [groups]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int v = blockIdx.y;
-    const int t0 = blockIdx.x * tiles_per_cta;
-    const int t1 = min(num_tiles, t0 + tiles_per_cta);
+    const int wo = warp / kMB, m0 = (warp % kMB) * 16;    // this warp's offset in the group, rows
+    auto g_base = [&](int s) { return smem_u32(wg_smem) + (uint32_t)(s * Cfg::kStageBytes); };
+    auto f_base = [&](int s) { return g_base(s) + (uint32_t)Cfg::kGBytes; };
+    auto s_row = [&](int s) { return reinterpret_cast<int32_t *>(wg_smem + s * Cfg::kStageBytes + Cfg::kGBytes + OG * Cfg::kFBytes); };
+
+    // this CTA's share of the flattened (group, active tile) list, in group order
+    int total = 0;
+    for (int g = tid; g < groups; g += NT) s_cnt[g] = cnt[g];
+    __syncthreads();
+    for (int g = 0; g < groups; ++g) total += s_cnt[g];
+    const int per = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int f0 = min(total, (int)blockIdx.x * per), f1 = min(total, f0 + per);
+    int wg = 0, wk = f0;                                  // cursor: group, index inside the group
+    while (wg < groups && wk >= s_cnt[wg]) { wk -= s_cnt[wg]; ++wg; }
+    int left = f1 - f0;
+    auto next = [&](int &g, int &t) {                     // next work tile, g = -1 at the end
+        if (left <= 0) { g = -1; t = 0; return; }
+        while (wk >= s_cnt[wg]) { wk = 0; ++wg; }
+        g = wg;
+        t = __ldg(list + (int64_t)wg * num_tiles + wk);
+        ++wk;
+        --left;
+    };
+
+    // offsets of group g that some voxel of tile t has (bit o = offset g*OG + o)
+    auto active = [&](int g, int t) -> uint32_t {
+        if (g < 0) return 0u;
+        const int v0 = g * OG, ng = min(OG, V - v0);
+        const uint32_t *u = uni + (int64_t)t * MW;
+        const int w0 = v0 >> 5, sh = v0 & 31;
+        uint64_t bits = __ldg(u + w0);
+        if (w0 + 1 < MW) bits |= (uint64_t)__ldg(u + w0 + 1) << 32;
+        return (uint32_t)(bits >> sh) & ((1u << ng) - 1u);
+    };
+    // tile row r's voxel and its neighbours at the group's active offsets (threads r < 128)
+    int32_t row = -1, jn[OG];
+    uint32_t act_next = 0;
+    auto load_idx = [&](int g, int t) {
+        row = -1;
+#pragma unroll
+        for (int o = 0; o < OG; ++o) jn[o] = -1;
+        act_next = active(g, t);
+        if (g < 0 || tid >= kWgTile) return;
+        const int64_t p = (int64_t)t * kWgTile + tid;
+        if (p >= M) return;
+        const int32_t rr = order ? __ldg(order + p) : (int32_t)p;
+        if ((uint32_t)rr >= (uint32_t)M) return;
+        row = rr;
+        const int v0 = g * OG, ng = min(OG, V - v0);
+        const int32_t *nr = nbr + (int64_t)rr * V + v0;
+#pragma unroll
+        for (int o = 0; o < OG; ++o) {
+            if (o < ng && ((act_next >> o) & 1u)) {
+                const int32_t jj = __ldg(nr + o);
+                jn[o] = (uint32_t)jj < (uint32_t)M ? jj : -1;
+            }
+        }
+    };
+    auto store_idx = [&](int s) {
+        if (tid < kWgTile) {
+            int32_t *sr = s_row(s);
+            sr[tid] = row;
+#pragma unroll
+            for (int o = 0; o < OG; ++o) sr[(1 + o) * kWgTile + tid] = jn[o];
+        }
+    };
+    auto gather = [&](int s, int g, uint32_t act) {       // after a barrier that published stage s's indices
+        const int32_t *sr = s_row(s);
+        const int ng = __popc(act);                       // feature tiles only for the active offsets
+        constexpr int kGC = CO / 8, kFC = CI / 8;
+        const uint32_t gb = g_base(s), fb = f_base(s);
+        for (int e = tid; e < kWgTile * kGC; e += NT) {
+            const int r = e / kGC, c = e - r * kGC;
+            const int32_t rr = sr[r];
+            cp_async_16(gb + (uint32_t)((r * GP + c * 8) * 2), gout + (int64_t)(rr >= 0 ? rr : 0) * CO + c * 8,
+                        rr >= 0 ? 16u : 0u);
+        }
+        for (int e = tid; e < ng * kWgTile * kFC; e += NT) {
+            const int c = e % kFC, r = (e / kFC) % kWgTile, k = e / (kFC * kWgTile);
+            uint32_t m = act;                             // the k-th active offset of the group
+            for (int i = 0; i < k; ++i) m &= m - 1u;
+            const int o = __ffs(m) - 1;
+            const int32_t jj = sr[(1 + o) * kWgTile + r];
+            cp_async_16(fb + (uint32_t)(k * Cfg::kFBytes + (r * FP + c * 8) * 2),
+                        feats + (int64_t)(jj >= 0 ? jj : 0) * CI + c * 8, jj >= 0 ? 16u : 0u);
+        }
+    };
 
     float acc[kNT][4];
 #pragma unroll
     for (int n = 0; n < kNT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    int cur_g = -1;
+    auto flush = [&]() {
+        if (cur_g < 0) return;
+        const int ng = min(OG, V - cur_g * OG);
+        if (wo < ng) {
+            // acc[n]: (co = m0 + g, ci = 8n + 2c, +1) and (co = m0 + g + 8, same ci)
+            const int gr = lane >> 2, c = lane & 3, v = cur_g * OG + wo;
+#pragma unroll
+            for (int n = 0; n < kNT; ++n) {
+                const int ci = n * 8 + 2 * c;
+                float *w0 = gw + ((int64_t)(m0 + gr) * V + v) * CI + ci;
+                float *w1 = gw + ((int64_t)(m0 + gr + 8) * V + v) * CI + ci;
+                if (acc[n][0] != 0.f) atomicAdd(w0, acc[n][0]);
+                if (acc[n][1] != 0.f) atomicAdd(w0 + 1, acc[n][1]);
+                if (acc[n][2] != 0.f) atomicAdd(w1, acc[n][2]);
+                if (acc[n][3] != 0.f) atomicAdd(w1 + 1, acc[n][3]);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < kNT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    };
 
-    const uint32_t g_base = smem_u32(Gs), f_base = smem_u32(Fs);
-    for (int t = t0; t < t1; ++t) {
-        // thread r < 128 owns tile row r: its voxel and that voxel's neighbour at offset v
-        static_assert(kThreads >= kWgTile, "one tile row per thread");
-        int32_t row = -1, j = -1;
-        if (tid < kWgTile) {
-            const int64_t p = (int64_t)t * kWgTile + tid;
-            if (p < M) {
-                row = order ? __ldg(order + p) : (int32_t)p;
-                if ((uint32_t)row < (uint32_t)M) {
-                    j = __ldg(nbr + (int64_t)row * V + v);
-                    if ((uint32_t)j >= (uint32_t)M) j = -1;
-                } else {
-                    row = -1;
+    // two-stage pipeline: tile k+1's rows are in flight while tile k is multiplied, and tile
+    // k+2's indices load meanwhile
+    int gA, tA, gB, tB, gC, tC;
+    next(gA, tA);
+    next(gB, tB);
+    load_idx(gA, tA);
+    uint32_t aA = act_next;
+    store_idx(0);
+    __syncthreads();
+    if (gA >= 0) gather(0, gA, aA);
+    cp_async_commit();
+    load_idx(gB, tB);
+    uint32_t aB = act_next;
+    for (int k = 0; gA >= 0; ++k) {
+        const int s = k & 1;
+        store_idx(s ^ 1);                                 // tile k+1's indices
+        __syncthreads();                                  // published; stage s^1 is free
+        if (gB >= 0) gather(s ^ 1, gB, aB);
+        cp_async_commit();
+        next(gC, tC);
+        load_idx(gC, tC);                                 // tile k+2's indices load meanwhile
+        const uint32_t aC = act_next;
+        cp_async_wait<1>();                               // tile k's rows have landed
+        __syncthreads();
+        if (gA != cur_g) { flush(); cur_g = gA; }
+        if ((aA >> wo) & 1u) {                            // this warp's offset is active in the tile
+            const int slot = __popc(aA & ((1u << wo) - 1u));      // its feature tile among the active ones
+            const uint32_t gb = g_base(s), fb = f_base(s) + (uint32_t)(slot * Cfg::kFBytes);
+            const int q = lane >> 3, rr = lane & 7;
+#pragma unroll 2
+            for (int k0 = 0; k0 < kWgTile; k0 += 16) {
+                // A = grad_out^T (m = co, k = voxel) from G[k][m]: matrices (k0|k0+8) x (m0|m0+8)
+                uint32_t a[4];
+                ldmatrix_x4_trans(a, gb + (uint32_t)(((k0 + rr + (q >> 1) * 8) * GP + m0 + (q & 1) * 8) * 2));
+#pragma unroll
+                for (int n = 0; n < kNT; n += 2) {
+                    // B^T = feats (n = ci, k = voxel) from F[k][n]: two n8 tiles per ldmatrix.x4
+                    uint32_t b[4];
+                    ldmatrix_x4_trans(b, fb + (uint32_t)(((k0 + rr + (q & 1) * 8) * FP + n * 8 + (q >> 1) * 8) * 2));
+                    mma_kind<T>::mma(acc[n], a, b[0], b[1]);
+                    mma_kind<T>::mma(acc[n + 1], a, b[2], b[3]);
                 }
             }
         }
-        if (!__syncthreads_or(j >= 0)) continue;          // no voxel of the tile has this neighbour
-        // gather: row r's grad_out into Gs[r], its neighbour's feats into Fs[r] (zeros if none)
-        if (tid < kWgTile) {
-            const int r = tid;
-            const bool have = j >= 0;
-            const T *gsrc = gout + (int64_t)(have ? row : 0) * CO;
-            const T *fsrc = feats + (int64_t)(have ? j : 0) * CI;
-#pragma unroll
-            for (int c = 0; c < CO / 8; ++c)
-                cp_async_16(g_base + (uint32_t)((r * GP + c * 8) * 2), gsrc + c * 8, have ? 16u : 0u);
-#pragma unroll
-            for (int c = 0; c < CI / 8; ++c)
-                cp_async_16(f_base + (uint32_t)((r * FP + c * 8) * 2), fsrc + c * 8, have ? 16u : 0u);
-        }
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-        const int m0 = warp * 16;
-#pragma unroll 2
-        for (int k0 = 0; k0 < kWgTile; k0 += 16) {
-            // A = grad_out^T (m = co, k = voxel) from Gs[k][m]: matrices (k0|k0+8) x (m0|m0+8)
-            uint32_t a[4];
-            {
-                const int q = lane >> 3, rr = lane & 7;
-                const int kk = k0 + rr + (q >> 1) * 8, mm = m0 + (q & 1) * 8;
-                ldmatrix_x4_trans(a, g_base + (uint32_t)((kk * GP + mm) * 2));
-            }
-#pragma unroll
-            for (int n = 0; n < kNT; n += 2) {
-                // B^T = feats (n = ci, k = voxel) from Fs[k][n]: two n8 tiles per ldmatrix.x4
-                uint32_t b[4];
-                const int q = lane >> 3, rr = lane & 7;
-                const int kk = k0 + rr + (q & 1) * 8, nn = n * 8 + (q >> 1) * 8;
-                ldmatrix_x4_trans(b, f_base + (uint32_t)((kk * FP + nn) * 2));
-                mma_kind<T>::mma(acc[n], a, b[0], b[1]);
-                mma_kind<T>::mma(acc[n + 1], a, b[2], b[3]);
-            }
-        }
-        __syncthreads();                                  // Gs/Fs are rewritten by the next tile
+        gA = gB; tA = tB; aA = aB;
+        gB = gC; tB = tC; aB = aC;
     }
-    // acc[n]: (co = m0 + g, ci = 8n + 2c, +1) and (co = m0 + g + 8, same ci)
-    const int g = lane >> 2, c = lane & 3, m0 = warp * 16;
-#pragma unroll
-    for (int n = 0; n < kNT; ++n) {
-        const int ci = n * 8 + 2 * c;
-        float *w0 = gw + ((int64_t)(m0 + g) * V + v) * CI + ci;
-        float *w1 = gw + ((int64_t)(m0 + g + 8) * V + v) * CI + ci;
-        if (acc[n][0] != 0.f) atomicAdd(w0, acc[n][0]);
-        if (acc[n][1] != 0.f) atomicAdd(w0 + 1, acc[n][1]);
-        if (acc[n][2] != 0.f) atomicAdd(w1, acc[n][2]);
-        if (acc[n][3] != 0.f) atomicAdd(w1 + 1, acc[n][3]);
-    }
-    (void)kWarps;
+    cp_async_wait<0>();
+    flush();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -194,9 +363,9 @@ wgrad_simt_kernel(const T *__restrict__ feats, const T *__restrict__ gout,
     extern __shared__ float ws_smem[];
     float *Gs = ws_smem;                                  // [kWsVox][Co]
     float *Fs = ws_smem + kWsVox * Co;                    // [kWsVox][Ci]
-    __shared__ int32_t s_row[kWsVox], s_nbr[kWsVox];
-    __shared__ int s_cnt;
-    const int tid = threadIdx.x;
+    __shared__ int32_t s_row[kWsThreads], s_nbr[kWsThreads];
+    __shared__ int s_wcnt[kWsThreads / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int v = blockIdx.y;
     const int64_t i0 = (int64_t)blockIdx.x * vox_per_cta;
     const int64_t i1 = min(M, i0 + vox_per_cta);
@@ -205,41 +374,52 @@ wgrad_simt_kernel(const T *__restrict__ feats, const T *__restrict__ gout,
         float acc[kWsOut];
 #pragma unroll
         for (int k = 0; k < kWsOut; ++k) acc[k] = 0.f;
-        for (int64_t b = i0; b < i1; b += kWsVox) {
-            // compact the batch's voxels that have a neighbour at offset v
-            if (tid == 0) s_cnt = 0;
-            __syncthreads();
-            if (tid < kWsVox && b + tid < i1) {
-                const int32_t jn = __ldg(nbr + (b + tid) * V + v);
-                if ((uint32_t)jn < (uint32_t)M) {
-                    const int slot = atomicAdd(&s_cnt, 1);
-                    s_row[slot] = (int32_t)(b + tid);
-                    s_nbr[slot] = jn;
-                }
+        for (int64_t b = i0; b < i1; b += kWsThreads) {
+            // the voxels of this batch that have a neighbour at offset v, compacted in order
+            int32_t jn = -1;
+            if (b + tid < i1) {
+                jn = __ldg(nbr + (b + tid) * V + v);
+                if ((uint32_t)jn >= (uint32_t)M) jn = -1;
             }
+            const uint32_t bal = __ballot_sync(0xffffffffu, jn >= 0);
+            if (lane == 0) s_wcnt[warp] = __popc(bal);
             __syncthreads();
-            const int n = s_cnt;
-            if (n == 0) continue;                         // uniform: s_cnt read after the barrier
-            for (int e = tid; e < n * Co; e += kWsThreads) {
-                const int s = e / Co, co = e - s * Co;
-                Gs[s * Co + co] = dtype_traits<T>::to_f(__ldg(gout + (int64_t)s_row[s] * Co + co));
-            }
-            for (int e = tid; e < n * Ci; e += kWsThreads) {
-                const int s = e / Ci, ci = e - s * Ci;
-                Fs[s * Ci + ci] = dtype_traits<T>::to_f(__ldg(feats + (int64_t)s_nbr[s] * Ci + ci));
-            }
-            __syncthreads();
+            int off = 0, n = 0;
 #pragma unroll
-            for (int k = 0; k < kWsOut; ++k) {
-                const int o = o0 + k * kWsThreads + tid;
-                if (o < nout) {
-                    const int co = o / Ci, ci = o - co * Ci;
-                    float a = acc[k];
-                    for (int s = 0; s < n; ++s) a = fmaf(Gs[s * Co + co], Fs[s * Ci + ci], a);
-                    acc[k] = a;
-                }
+            for (int w = 0; w < kWsThreads / 32; ++w) {
+                const int c = s_wcnt[w];
+                off += w < warp ? c : 0;
+                n += c;
+            }
+            if (jn >= 0) {
+                const int slot = off + __popc(bal & ((1u << lane) - 1u));
+                s_row[slot] = (int32_t)(b + tid);
+                s_nbr[slot] = jn;
             }
             __syncthreads();
+            for (int s0 = 0; s0 < n; s0 += kWsVox) {
+                const int ns = min(kWsVox, n - s0);
+                for (int e = tid; e < ns * Co; e += kWsThreads) {
+                    const int sv = e / Co, co = e - sv * Co;
+                    Gs[sv * Co + co] = dtype_traits<T>::to_f(__ldg(gout + (int64_t)s_row[s0 + sv] * Co + co));
+                }
+                for (int e = tid; e < ns * Ci; e += kWsThreads) {
+                    const int sv = e / Ci, ci = e - sv * Ci;
+                    Fs[sv * Ci + ci] = dtype_traits<T>::to_f(__ldg(feats + (int64_t)s_nbr[s0 + sv] * Ci + ci));
+                }
+                __syncthreads();
+#pragma unroll
+                for (int k = 0; k < kWsOut; ++k) {
+                    const int o = o0 + k * kWsThreads + tid;
+                    if (o < nout) {
+                        const int co = o / Ci, ci = o - co * Ci;
+                        float a = acc[k];
+                        for (int sv = 0; sv < ns; ++sv) a = fmaf(Gs[sv * Co + co], Fs[sv * Ci + ci], a);
+                        acc[k] = a;
+                    }
+                }
+                __syncthreads();
+            }
         }
 #pragma unroll
         for (int k = 0; k < kWsOut; ++k) {
@@ -265,46 +445,71 @@ bias_grad_kernel(const T *__restrict__ gout, int64_t M, int Co, int64_t rows_per
     }
 }
 
+// Scratch of the weight gradient: tile unions [num_tiles][MW], group lists [V][num_tiles],
+// group counts [V].
+static int64_t wgrad_scratch_bytes(int64_t M, int V) {
+    const int64_t nt = (M + kWgTile - 1) / kWgTile;
+    const int64_t MW = (V + 31) / 32;
+    return 4 * (nt * MW + (int64_t)V * nt + V) + 256;
+}
+
 template <typename T, int CO, int CI>
-static int launch_wgrad_mma(const void *feats, const void *gout, const int32_t *nbr, const int32_t *order,
-                            int64_t M, int V, float *gw, cudaStream_t stream) {
+static int launch_wgrad_mma(const void *feats, const void *gout, const int32_t *nbr, const uint32_t *masks,
+                            const int32_t *order, int64_t M, int V, float *gw, void *scratch, cudaStream_t stream) {
+    using Cfg = WgCfg<T, CO, CI>;
     auto kern = wgrad_mma_kernel<T, CO, CI>;
-    const int smem = kWgTile * ((CO + 8) + (CI + 8)) * (int)sizeof(T);
     static bool attr_done[64] = {false};
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
             return check_launch("wgrad: set max dynamic shared memory");
         attr_done[dev] = true;
     }
-    const int num_tiles = (int)((M + kWgTile - 1) / kWgTile);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // about eight CTAs per SM over all offsets; each CTA adds its accumulators once
-    int64_t want = (int64_t)sms * 8 / V;
-    if (want < 1) want = 1;
-    int tiles_per_cta = (int)((num_tiles + want - 1) / want);
-    if (tiles_per_cta < 1) tiles_per_cta = 1;
-    const int gx = (num_tiles + tiles_per_cta - 1) / tiles_per_cta;
-    kern<<<dim3(gx, V), CO * 2, smem, stream>>>((const T *)feats, (const T *)gout, nbr, order, M, V,
-                                               num_tiles, tiles_per_cta, gw);
+    const int num_tiles = (int)((M + kWgTile - 1) / kWgTile);
+    const int groups = (V + Cfg::OG - 1) / Cfg::OG;
+    const int MW = (V + 31) / 32;
+    uint32_t *uni = (uint32_t *)scratch;
+    int32_t *list = (int32_t *)(uni + (int64_t)num_tiles * MW);
+    int32_t *cnt = list + (int64_t)V * num_tiles;
+    tile_union_kernel<<<num_tiles, kWgTile, 0, stream>>>(MW <= 4 ? masks : nullptr, nbr, order, M, V, MW, uni);
+    if (int rc = check_launch("tile_union_kernel")) return rc;
+    group_tiles_kernel<<<groups, 512, 0, stream>>>(uni, num_tiles, MW, V, Cfg::OG, list, cnt);
+    if (int rc = check_launch("group_tiles_kernel")) return rc;
+    static int occ_cache[64] = {0};
+    if (occ_cache[dev] == 0) {
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, Cfg::kThreads, Cfg::kSmem) != cudaSuccess || occ < 1)
+            occ = 1;
+        occ_cache[dev] = occ;
+    }
+    kern<<<sms * occ_cache[dev], Cfg::kThreads, Cfg::kSmem, stream>>>(
+        (const T *)feats, (const T *)gout, nbr, order, list, cnt, uni, MW, M, V, num_tiles, groups, gw);
     return check_launch("wgrad_mma_kernel");
 }
 
 template <typename T>
-static int launch_wgrad_t(const void *feats, const void *gout, const int32_t *nbr, const int32_t *order,
-                          int64_t M, int V, int Ci, int Co, float *gw, float *gb, cudaStream_t stream) {
+static int launch_wgrad_t(const void *feats, const void *gout, const int32_t *nbr, const uint32_t *masks,
+                          const int32_t *order, int64_t M, int V, int Ci, int Co, float *gw, float *gb,
+                          void *scratch, cudaStream_t stream) {
     int rc = SPCONV_OK;
     bool done = false;
     if constexpr (!std::is_same<T, float>::value) {
-        if (((uintptr_t)feats & 15u) == 0 && ((uintptr_t)gout & 15u) == 0) {
+        static_assert(kWgMaxGroups >= 1024, "group counts of any kernel volume fit in shared memory");
+        if (((uintptr_t)feats & 15u) == 0 && ((uintptr_t)gout & 15u) == 0 && scratch) {
 #define SPCONV_WG(CO_, CI_)                                                                  \
-            if (!done && Co == CO_ && Ci == CI_) {                                           \
-                rc = launch_wgrad_mma<T, CO_, CI_>(feats, gout, nbr, order, M, V, gw, stream); \
-                done = true;                                                                 \
+            if constexpr (WgCfg<T, CO_, CI_>::kSupported) {                                  \
+                if (!done && Co == CO_ && Ci == CI_) {                                       \
+                    rc = launch_wgrad_mma<T, CO_, CI_>(feats, gout, nbr, masks, order, M, V, gw, scratch, stream); \
+                    done = true;                                                             \
+                }                                                                            \
             }
-            SPCONV_WG(64, 64) SPCONV_WG(64, 128) SPCONV_WG(128, 64) SPCONV_WG(128, 128)
+            SPCONV_WG(16, 16) SPCONV_WG(16, 32) SPCONV_WG(16, 64) SPCONV_WG(16, 128)
+            SPCONV_WG(32, 16) SPCONV_WG(32, 32) SPCONV_WG(32, 64) SPCONV_WG(32, 128)
+            SPCONV_WG(64, 16) SPCONV_WG(64, 32) SPCONV_WG(64, 64) SPCONV_WG(64, 128)
+            SPCONV_WG(128, 16) SPCONV_WG(128, 32) SPCONV_WG(128, 64) SPCONV_WG(128, 128)
 #undef SPCONV_WG
         }
     }
@@ -354,10 +559,15 @@ extern "C" int spconv_transpose_neighbor_map(const int32_t *nbr, int64_t M, int 
     return SPCONV_OK;
 }
 
+extern "C" int64_t spconv_weight_grad_workspace_bytes(int64_t num_coords, int kernel_volume) {
+    if (num_coords < 0 || kernel_volume <= 0 || kernel_volume > 1024) return -1;
+    return wgrad_scratch_bytes(num_coords, kernel_volume);
+}
+
 extern "C" int spconv_submanifold_conv_weight_grad(
     const void *feats, const void *grad_out, int dtype, int64_t M, int Ci, int Co, int V,
-    const int32_t *nbr, const int32_t *order, float *grad_weight, float *grad_bias,
-    int32_t *status, void *stream) {
+    const int32_t *nbr, const uint32_t *masks, const int32_t *order, float *grad_weight, float *grad_bias,
+    void *workspace, int64_t workspace_bytes, int32_t *status, void *stream) {
     (void)status;
     SPCONV_REQUIRE(M >= 0 && M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld out of range", (long long)M);
     SPCONV_REQUIRE(Ci > 0 && Co > 0, SPCONV_ERR_ARG, "channels must be positive (Ci=%d Co=%d)", Ci, Co);
@@ -372,9 +582,15 @@ extern "C" int spconv_submanifold_conv_weight_grad(
         return check_launch("grad_bias memset");
     if (M == 0) return SPCONV_OK;
     SPCONV_REQUIRE(feats && grad_out && nbr, SPCONV_ERR_ARG, "null pointer argument");
+    SPCONV_REQUIRE(workspace == nullptr || ((uintptr_t)workspace & 15u) == 0, SPCONV_ERR_ARG,
+                   "workspace must be 16-byte aligned");
+    void *scratch = (workspace && workspace_bytes >= wgrad_scratch_bytes(M, V)) ? workspace : nullptr;
     switch (dtype) {
-        case SPCONV_F32: return launch_wgrad_t<float>(feats, grad_out, nbr, order, M, V, Ci, Co, grad_weight, grad_bias, s);
-        case SPCONV_F16: return launch_wgrad_t<__half>(feats, grad_out, nbr, order, M, V, Ci, Co, grad_weight, grad_bias, s);
-        default: return launch_wgrad_t<__nv_bfloat16>(feats, grad_out, nbr, order, M, V, Ci, Co, grad_weight, grad_bias, s);
+        case SPCONV_F32:
+            return launch_wgrad_t<float>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, s);
+        case SPCONV_F16:
+            return launch_wgrad_t<__half>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, s);
+        default:
+            return launch_wgrad_t<__nv_bfloat16>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, s);
     }
 }

@@ -53,9 +53,10 @@ SIGNATURES = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_transpose_neighbor_map": (_c_int, [
         _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_weight_grad_workspace_bytes": (_c_i64, [_c_i64, _c_int]),
     "spconv_submanifold_conv_weight_grad": (_c_int, [
         _c_void_p, _c_void_p, _c_int, _c_i64, _c_int, _c_int, _c_int,
-        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
     "spconv_stage_timing": (_c_int, [_c_int]),
     "spconv_stage_times_ms": (_c_int, [_c_void_p, _c_void_p, _c_int]),
 }
@@ -344,12 +345,13 @@ def transpose_neighbor_map(nbr: torch.Tensor) -> Tuple[torch.Tensor, torch.Tenso
 
 
 def conv_weight_grad(feats: torch.Tensor, grad_out: torch.Tensor, nbr: torch.Tensor,
-                     order: Optional[torch.Tensor], with_bias: bool = True
+                     order: Optional[torch.Tensor], with_bias: bool = True,
+                     masks: Optional[torch.Tensor] = None
                      ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """(grad_weight [Co, V, Ci] fp32, grad_bias [Co] fp32 or None) of the submanifold conv:
     grad_weight[co, v, ci] = sum_i grad_out[i, co] * feats[nbr[i, v], ci]."""
     lib = load_library()
-    dev = _require_cuda(feats, grad_out, nbr, order)
+    dev = _require_cuda(feats, grad_out, nbr, order, masks)
     if feats.dtype not in DTYPE_CODES:
         raise TypeError(f"unsupported feature dtype {feats.dtype}")
     if grad_out.dtype != feats.dtype:
@@ -365,14 +367,21 @@ def conv_weight_grad(feats: torch.Tensor, grad_out: torch.Tensor, nbr: torch.Ten
         raise ValueError("feats, grad_out and neighbor map must have the same number of rows")
     if order is not None and (order.dtype != torch.int32 or order.numel() != M or not order.is_contiguous()):
         raise ValueError("order must be a contiguous [M] int32 tensor")
+    mk = None
+    if masks is not None:
+        mk = masks.view(torch.int32) if masks.dtype == torch.uint32 else masks
+        if mk.dtype != torch.int32 or mk.shape[0] != M or not mk.is_contiguous():
+            raise ValueError("masks must be a contiguous [M, ceil(V/32)] 32-bit tensor")
     gw = torch.empty((Co, V, Ci), dtype=torch.float32, device=dev)
     gb = torch.empty((Co,), dtype=torch.float32, device=dev) if with_bias else None
+    ws_bytes = int(lib.spconv_weight_grad_workspace_bytes(M, V))
+    ws = torch.empty((max(ws_bytes, 16) + 15) // 16 * 16, dtype=torch.uint8, device=dev)
     before_launch(dev)
     st = status_word(dev)
     rc = lib.spconv_submanifold_conv_weight_grad(
         feats.data_ptr(), grad_out.data_ptr(), DTYPE_CODES[feats.dtype], M, Ci, Co, V, nb.data_ptr(),
-        None if order is None else order.data_ptr(), gw.data_ptr(),
-        None if gb is None else gb.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
+        None if mk is None else mk.data_ptr(), None if order is None else order.data_ptr(), gw.data_ptr(),
+        None if gb is None else gb.data_ptr(), ws.data_ptr(), ws.numel(), st.word.data_ptr(), _stream_ptr(dev))
     if rc != SPCONV_OK:
         _raise(rc, "spconv_submanifold_conv_weight_grad")
     return gw, gb

@@ -155,7 +155,7 @@ class SubMConv3dFunction(Function):
                      bias is not None and bias.requires_grad)
         Co, Kw, Kh, Kd, Ci = weight.shape
         V = Kw * Kh * Kd
-        nbr, _masks, order = _cache_tensors(neighbor_cache)
+        nbr, masks, order = _cache_tensors(neighbor_cache)
         g = grad_output.to(feats.dtype).contiguous()
         grad_input = grad_weight = grad_bias = None
         if needs[0]:
@@ -168,7 +168,7 @@ class SubMConv3dFunction(Function):
             grad_input = _native.conv_forward(g, w_t, None, nbr_t, masks_t, order)
         if needs[1] or (bias is not None and needs[2]):
             gw, gb = _native.conv_weight_grad(feats.contiguous(), g, nbr, order,
-                                              with_bias=bias is not None and needs[2])
+                                              with_bias=bias is not None and needs[2], masks=masks)
             if needs[1]:
                 grad_weight = gw.view(Co, Kw, Kh, Kd, Ci).to(weight.dtype)
             if gb is not None:
