@@ -113,6 +113,16 @@ def _traffic_per_launch(key: str):
     return None
 
 
+def _launches_per_step(M: int, V: int) -> int:
+    """Kernels one forward launches: insert, map, order (one bucket scatter, or three per 8-bit
+    radix pass for maps of >= 2^19 voxels of <= 27-offset kernels), conv."""
+    if M >= (1 << 19) and V <= 27:
+        drop = max(V - 21, 0)
+        passes = (4 + V - 1 - drop + 7) // 8
+        return 2 + 3 * passes + 1
+    return 4
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -207,6 +217,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-backward", action="store_true", help="skip the training-step (forward + backward) figure")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run this many eager forwards of the workload and exit (a target for ncu)")
     args = ap.parse_args()
@@ -383,6 +394,39 @@ def main():
     e2e_value = voxels_all * KE / (e2e_ms / 1e3)
     _native.check_errors(dev)
 
+    # ---------------- training step: map build + forward + backward through autograd ----------------
+    # Eager (autograd runs between the kernels); every step builds its own map (and so its own
+    # transposed map) and computes the input and weight gradients; L2 flushed between steps.
+    train = None
+    if not args.no_backward:
+        f_req = feats.detach().clone().requires_grad_(True)
+        w_req = weight.detach().clone().requires_grad_(True)
+        g_out_t = torch.randn(out.shape, generator=torch.Generator().manual_seed(3)).to(out.dtype).to(dev)
+
+        def train_step():
+            o, _c = sparse_submanifold_conv3d(f_req, coords, shape, w_req, algorithm=Algorithm.IMPLICIT_GEMM)
+            o.backward(g_out_t)
+
+        for _ in range(args.warmup):
+            train_step()
+        KT = max(3, min(K, 20))
+        t_s = [torch.cuda.Event(enable_timing=True) for _ in range(KT)]
+        t_e = [torch.cuda.Event(enable_timing=True) for _ in range(KT)]
+        torch.cuda.synchronize()
+        if pg is not None:
+            torch.distributed.barrier()
+        for i in range(KT):
+            flush.fill_(i)
+            t_s[i].record(stream)
+            train_step()
+            t_e[i].record(stream)
+        torch.cuda.synchronize()
+        _native.check_errors(dev)
+        train_ms = shards.max_over_ranks(float(sum(a.elapsed_time(b) for a, b in zip(t_s, t_e))))
+        train = {"value": voxels_all * KT / (train_ms / 1e3), "unit": UNIT, "ms_per_step": train_ms / KT,
+                 "steps": KT, "step": "eager map build + forward + backward (input and weight gradients) "
+                                      "through autograd, fresh map each step"}
+
     if rank == 0:
         hbm, tc, peak_kind = _peaks()
         # dominant kernel by live stage time
@@ -414,9 +458,11 @@ def main():
                     "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()), "steps": KE,
                     "pipelined": "two CUDA streams: step i+1's H2D overlaps step i's op and D2H",
                     "serial_value": e2e_serial},
-            "gpu_launches": 4 * K,
+            "gpu_launches": _launches_per_step(w.num_voxels, int(np.prod(w.kernel_size))) * K,
             "clocks": clk,
         }
+        if train is not None:
+            line["training_step"] = train
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)
         print(json.dumps(line), flush=True)
