@@ -101,6 +101,39 @@ int spconv_build_submanifold_neighbor_map(
     int32_t *neighbor_map, uint32_t *masks, int32_t *order,
     int32_t *status, void *stream);
 
+/* Workspace (bytes) for spconv_build_submanifold_neighbor_map_2d. */
+int64_t spconv_neighbor_map_2d_workspace_bytes(int64_t num_coords, int batch, int W, int H);
+
+/* 2-D submanifold kernel map: coords [M,3] int32 (b, x, y) on a batch x W x H grid, kernel
+ * Kw x Kh, dilation Dw x Dh; neighbor_map [M, Kw*Kh] with v = dx*Kh + dy, -1 = missing,
+ * v == V/2 the voxel's own row; masks / order as for the 3-D map. The reference's 2-D map is
+ * its 3-D map with D = 1, Kd = 1, z = 0 (same offsets, centre rule and keys), and so is this.
+ * Replaces hashmap_build_submanifold_conv2d_neighbor_map_cuda_naive (neighbor_map.h:4-14,
+ * neighbor_map.cu:10-111). */
+int spconv_build_submanifold_neighbor_map_2d(
+    const int32_t *coords, int64_t num_coords, int batch, int W, int H,
+    int Kw, int Kh, int Dw, int Dh,
+    void *workspace, int64_t workspace_bytes,
+    int32_t *neighbor_map, uint32_t *masks, int32_t *order,
+    int32_t *status, void *stream);
+
+/* Dense <-> sparse conversion (SparseConvTensor.from_dense / .dense, core.py:52-77).
+ * spconv_from_dense: a voxel of the channels-last dense [batch, W, H, D, C] tensor is active
+ * iff any of its C values is non-zero (x != 0: NaN counts, -0 does not). Phase 0 writes the
+ * number of active voxels to *count (device int64); the caller reads it, allocates indices
+ * [count, 4] int32 (16-byte aligned) and feats [count, C], and calls phase 1, which writes
+ * (b, x, y, z) and the features in (b, x, y, z) order. The workspace
+ * (spconv_from_dense_workspace_bytes) must be the same for both phases.
+ * spconv_to_dense: zeroes out [batch, C, W, H, D] (channels_first) or [batch, W, H, D, C] and
+ * writes feats [M, C] at indices [M, 4]; indices outside the grid set SPCONV_STATUS_COORD_RANGE. */
+int64_t spconv_from_dense_workspace_bytes(int batch, int W, int H, int D);
+int spconv_from_dense(const void *dense, int dtype, int batch, int W, int H, int D, int C,
+                      void *workspace, int64_t workspace_bytes, int64_t *count,
+                      int32_t *indices, void *feats, int64_t capacity, int phase, void *stream);
+int spconv_to_dense(const void *feats, int dtype, const int32_t *indices, int64_t num_coords, int C,
+                    int batch, int W, int H, int D, int channels_first, void *out,
+                    int32_t *status, void *stream);
+
 /* Largest num_coords that spconv_build_submanifold_neighbor_map_noalloc accepts. */
 #define SPCONV_NOALLOC_MAX_COORDS 262144
 

@@ -262,7 +262,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     long long *s_delta = reinterpret_cast<long long *>(s_off + V);   // [V] flat-key deltas
     int32_t *s_stage = reinterpret_cast<int32_t *>(s_delta + V);     // [kMapThreads][vstride]
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const int64_t i0 = (int64_t)blockIdx.x * kMapThreads;
     const int nvox = (M - i0) < (int64_t)kMapThreads ? (int)(M - i0) : kMapThreads;
     const bool staged = vstride > 0;
@@ -1355,4 +1355,52 @@ extern "C" int spconv_build_submanifold_neighbor_map_noalloc(
     return spconv_build_submanifold_neighbor_map(
         coords, M, batch, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, scratch, kNoAllocScratchBytes,
         neighbor_map, masks, order, status, stream);
+}
+
+// ---------------------------------------------------------------------------------------
+// 2-D submanifold map (replaces hashmap_build_submanifold_conv2d_neighbor_map_cuda_naive,
+// neighbor_map.cu:10-111): (b, x, y) coordinates on a W x H grid with a Kw x Kh kernel. Its
+// offset order v = dx * Kh + dy, centre rule v == V/2 and flat key b*W*H + x*H + y are those
+// of the 3-D map with D = 1, Kd = 1 and z = 0, so the coordinates are widened to (b, x, y, 0)
+// in the workspace and the 3-D builder runs on them.
+// ---------------------------------------------------------------------------------------
+namespace spconv {
+
+__global__ void __launch_bounds__(256)
+widen_coords_2d_kernel(const int32_t *__restrict__ c3, int64_t M, int4 *__restrict__ c4) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M; i += (int64_t)gridDim.x * blockDim.x)
+        c4[i] = make_int4(__ldg(c3 + 3 * i), __ldg(c3 + 3 * i + 1), __ldg(c3 + 3 * i + 2), 0);
+}
+
+static int64_t coords4_bytes(int64_t M) { return align256(M * 16); }
+
+}  // namespace spconv
+
+extern "C" int64_t spconv_neighbor_map_2d_workspace_bytes(int64_t num_coords, int batch, int W, int H) {
+    if (num_coords < 0) return -1;
+    const int64_t b3 = spconv_neighbor_map_workspace_bytes(num_coords, batch, W, H, 1);
+    return b3 < 0 ? -1 : b3 + coords4_bytes(num_coords);
+}
+
+extern "C" int spconv_build_submanifold_neighbor_map_2d(
+    const int32_t *coords, int64_t M, int batch, int W, int H, int Kw, int Kh, int Dw, int Dh,
+    void *workspace, int64_t workspace_bytes,
+    int32_t *neighbor_map, uint32_t *masks, int32_t *order, int32_t *status, void *stream) {
+    SPCONV_REQUIRE(M >= 0, SPCONV_ERR_ARG, "num_coords must be >= 0 (got %lld)", (long long)M);
+    if (M == 0) return SPCONV_OK;
+    SPCONV_REQUIRE(coords && workspace, SPCONV_ERR_ARG, "null pointer argument");
+    SPCONV_REQUIRE(((uintptr_t)workspace & 255u) == 0, SPCONV_ERR_ARG, "workspace must be 256-byte aligned");
+    const int64_t need = spconv_neighbor_map_2d_workspace_bytes(M, batch, W, H);
+    SPCONV_REQUIRE(need >= 0 && workspace_bytes >= need, SPCONV_ERR_ARG,
+                   "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
+    int4 *c4 = (int4 *)workspace;
+    cudaStream_t s = (cudaStream_t)stream;
+    int64_t blocks = (M + 255) / 256;
+    if (blocks > 148LL * 32) blocks = 148LL * 32;
+    widen_coords_2d_kernel<<<(unsigned)blocks, 256, 0, s>>>(coords, M, c4);
+    if (int rc = check_launch("widen_coords_2d_kernel")) return rc;
+    const int64_t off = coords4_bytes(M);
+    return spconv_build_submanifold_neighbor_map(
+        (const int32_t *)c4, M, batch, W, H, 1, Kw, Kh, 1, Dw, Dh, 1, (char *)workspace + off,
+        workspace_bytes - off, neighbor_map, masks, order, status, stream);
 }

@@ -51,6 +51,17 @@ SIGNATURES = {
         _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_neighbor_map_2d_workspace_bytes": (_c_i64, [_c_i64, _c_int, _c_int, _c_int]),
+    "spconv_build_submanifold_neighbor_map_2d": (_c_int, [
+        _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+        _c_void_p, _c_i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_from_dense_workspace_bytes": (_c_i64, [_c_int, _c_int, _c_int, _c_int]),
+    "spconv_from_dense": (_c_int, [
+        _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_i64, _c_void_p,
+        _c_void_p, _c_void_p, _c_i64, _c_int, _c_void_p]),
+    "spconv_to_dense": (_c_int, [
+        _c_void_p, _c_int, _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+        _c_void_p, _c_void_p, _c_void_p]),
     "spconv_transpose_neighbor_map": (_c_int, [
         _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_weight_grad_workspace_bytes": (_c_i64, [_c_i64, _c_int]),
@@ -267,6 +278,41 @@ def build_neighbor_map(coords: torch.Tensor, batch: int, W: int, H: int, D: int,
     return nbr, masks, order
 
 
+def build_neighbor_map_2d(coords: torch.Tensor, batch: int, W: int, H: int,
+                          kernel_size: Sequence[int], dilation: Sequence[int],
+                          ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """2-D kernel map of ``coords`` ([M,3] int32 (b, x, y) on CUDA): (neighbor_map [M, Kw*Kh]
+    int32, masks, order), the map of the reference's
+    ``hashmap_build_submanifold_conv2d_neighbor_map_cuda_naive`` (neighbor_map.cu:10-111)."""
+    lib = load_library()
+    dev = _require_cuda(coords)
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] != 3:
+        raise ValueError("coords must be an [M, 3] int32 tensor")
+    if not coords.is_contiguous():
+        raise ValueError("coords must be contiguous")
+    Kw, Kh = (int(k) for k in kernel_size)
+    Dw, Dh = (int(d) for d in dilation)
+    M = int(coords.shape[0])
+    V = Kw * Kh
+    nbr = torch.empty((M, V), dtype=torch.int32, device=dev)
+    masks = torch.empty((M, max(1, mask_words(V))), dtype=torch.int32, device=dev)
+    order = torch.empty((M,), dtype=torch.int32, device=dev)
+    if M == 0:
+        return nbr, masks, order
+    need = int(lib.spconv_neighbor_map_2d_workspace_bytes(M, int(batch), int(W), int(H)))
+    if need < 0:
+        raise ValueError("invalid 2-D map arguments")
+    workspace = torch.empty((need,), dtype=torch.uint8, device=dev)
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_build_submanifold_neighbor_map_2d(
+        coords.data_ptr(), M, int(batch), int(W), int(H), Kw, Kh, Dw, Dh, workspace.data_ptr(), need,
+        nbr.data_ptr(), masks.data_ptr(), order.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_build_submanifold_neighbor_map_2d")
+    return nbr, masks, order
+
+
 def conv_forward(feats: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
                  nbr: torch.Tensor, masks: Optional[torch.Tensor], order: Optional[torch.Tensor],
                  kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -320,6 +366,62 @@ def conv_forward(feats: torch.Tensor, weight: torch.Tensor, bias: Optional[torch
         out.data_ptr(), st.word.data_ptr(), _stream_ptr(dev), int(kernel))
     if rc != SPCONV_OK:
         _raise(rc, "spconv_submanifold_conv_forward")
+    return out
+
+
+def dense_to_sparse(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(indices [M,4] int32 (b,x,y,z), features [M,C]) of the voxels of a channels-last dense
+    [B, W, H, D, C] CUDA tensor with any non-zero channel, in (b, x, y, z) order. Reads the
+    number of active voxels back to the host (one synchronisation) to size the outputs."""
+    lib = load_library()
+    dev = _require_cuda(x)
+    if x.dtype not in DTYPE_CODES or x.dim() != 5:
+        raise ValueError("expected a [B, W, H, D, C] float32/float16/bfloat16 tensor")
+    x = x.contiguous()
+    B, W, H, D, C = (int(v) for v in x.shape)
+    if B * W * H * D == 0 or C == 0:
+        return (torch.empty((0, 4), dtype=torch.int32, device=dev),
+                torch.empty((0, C), dtype=x.dtype, device=dev))
+    need = int(lib.spconv_from_dense_workspace_bytes(B, W, H, D))
+    if need <= 0:
+        raise ValueError("dense tensor too large")
+    ws = torch.empty((need,), dtype=torch.uint8, device=dev)
+    count = torch.zeros((1,), dtype=torch.int64, device=dev)
+    stream = _stream_ptr(dev)
+    rc = lib.spconv_from_dense(x.data_ptr(), DTYPE_CODES[x.dtype], B, W, H, D, C, ws.data_ptr(), need,
+                               count.data_ptr(), None, None, 0, 0, stream)
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_from_dense")
+    M = int(count.item())
+    indices = torch.empty((M, 4), dtype=torch.int32, device=dev)
+    feats = torch.empty((M, C), dtype=x.dtype, device=dev)
+    rc = lib.spconv_from_dense(x.data_ptr(), DTYPE_CODES[x.dtype], B, W, H, D, C, ws.data_ptr(), need,
+                               count.data_ptr(), indices.data_ptr(), feats.data_ptr(), M, 1, stream)
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_from_dense")
+    return indices, feats
+
+
+def sparse_to_dense(feats: torch.Tensor, indices: torch.Tensor, batch: int, spatial: Sequence[int],
+                    channels_first: bool = True) -> torch.Tensor:
+    """Zero dense tensor [B, C, W, H, D] (or [B, W, H, D, C]) with the rows of ``feats`` at
+    ``indices`` ([M,4] int32 (b,x,y,z))."""
+    lib = load_library()
+    dev = _require_cuda(feats, indices)
+    if feats.dtype not in DTYPE_CODES:
+        raise TypeError(f"unsupported feature dtype {feats.dtype}")
+    feats = feats.contiguous()
+    idx = indices.to(torch.int32).contiguous()
+    M, C = int(feats.shape[0]), int(feats.shape[1])
+    W, H, D = (int(v) for v in spatial)
+    shape = (batch, C, W, H, D) if channels_first else (batch, W, H, D, C)
+    out = torch.empty(shape, dtype=feats.dtype, device=dev)
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_to_dense(feats.data_ptr(), DTYPE_CODES[feats.dtype], idx.data_ptr(), M, C, int(batch), W, H, D,
+                             1 if channels_first else 0, out.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_to_dense")
     return out
 
 

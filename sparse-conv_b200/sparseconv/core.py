@@ -51,7 +51,15 @@ class SparseConvTensor(metaclass=ProxyableClassMeta):
     @classmethod
     def from_dense(cls, x: torch.Tensor) -> "SparseConvTensor":
         """Channels-last dense [B, *spatial, C] -> sparse; a voxel is active iff any of
-        its channels is non-zero. Indices come out sorted by (b, x, y, z)."""
+        its channels is non-zero. Indices come out sorted by (b, x, y, z).
+
+        CUDA [B, W, H, D, C] float tensors go through the library's compaction kernels (one
+        host synchronisation for the voxel count); other inputs use torch's ``to_sparse`` as
+        the reference does (core.py:56-63)."""
+        if x.is_cuda and x.dim() == 5 and x.dtype in (torch.float32, torch.float16, torch.bfloat16):
+            from sparseconv import _native
+            indices, features = _native.dense_to_sparse(x)
+            return cls(features, indices, list(x.shape[1:4]), int(x.shape[0]))
         x_sp = x.to_sparse(x.ndim - 1)
         spatial_shape = x_sp.shape[1:-1]
         batch_size = x_sp.shape[0]
@@ -60,6 +68,13 @@ class SparseConvTensor(metaclass=ProxyableClassMeta):
         return cls(features, indices, spatial_shape, batch_size)
 
     def dense(self, channels_first: bool = True) -> torch.Tensor:
+        """Zero-filled dense tensor, [B, C, *spatial] (channels_first) or [B, *spatial, C]
+        (core.py:65-77); CUDA 3-D tensors are scattered by the library in the final layout."""
+        if (self.features.is_cuda and len(self.spatial_shape) == 3 and self.features.dim() == 2
+                and self.features.dtype in (torch.float32, torch.float16, torch.bfloat16)):
+            from sparseconv import _native
+            return _native.sparse_to_dense(self.features, self.indices.to(self.features.device),
+                                           int(self.batch_size), self.spatial_shape, channels_first)
         output_shape = [self.batch_size] + list(self.spatial_shape) + [self.features.shape[1]]
         res = scatter_nd(self.indices.to(self.features.device).long(), self.features, output_shape)
         if not channels_first:
