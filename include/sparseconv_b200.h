@@ -134,6 +134,20 @@ int spconv_to_dense(const void *feats, int dtype, const int32_t *indices, int64_
                     int batch, int W, int H, int D, int channels_first, void *out,
                     int32_t *status, void *stream);
 
+/* Generic caller-owned hash table (hashmap_insert_cuda / hashmap_lookup_cuda, hash.cu:8-146):
+ * table_keys [capacity] uint32/uint64 (key_bits), filled with all ones when empty;
+ * table_values [capacity] uint32/uint64 (value_bits). The slot of a key is the MurmurHash3
+ * finaliser of the key modulo capacity, probed linearly (the reference's layout and slots, so
+ * its tables read the same here and back). Insert stores values (a key given twice in one call
+ * keeps one of its values) and sets SPCONV_STATUS_TABLE_FULL in *status when no slot is left;
+ * lookup writes the value, or all ones for an absent key. Probing is bounded by capacity. */
+int spconv_hashmap_insert(void *table_keys, void *table_values, int64_t capacity, int key_bits,
+                          int value_bits, const void *keys, const void *values, int64_t n,
+                          int32_t *status, void *stream);
+int spconv_hashmap_lookup(const void *table_keys, const void *table_values, int64_t capacity,
+                          int key_bits, int value_bits, const void *keys, void *values_out, int64_t n,
+                          void *stream);
+
 /* Largest num_coords that spconv_build_submanifold_neighbor_map_noalloc accepts. */
 #define SPCONV_NOALLOC_MAX_COORDS 262144
 

@@ -62,6 +62,10 @@ SIGNATURES = {
     "spconv_to_dense": (_c_int, [
         _c_void_p, _c_int, _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
         _c_void_p, _c_void_p, _c_void_p]),
+    "spconv_hashmap_insert": (_c_int, [
+        _c_void_p, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
+    "spconv_hashmap_lookup": (_c_int, [
+        _c_void_p, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p, _c_i64, _c_void_p]),
     "spconv_transpose_neighbor_map": (_c_int, [
         _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_weight_grad_workspace_bytes": (_c_i64, [_c_i64, _c_int]),
@@ -422,6 +426,53 @@ def sparse_to_dense(feats: torch.Tensor, indices: torch.Tensor, batch: int, spat
                              1 if channels_first else 0, out.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
     if rc != SPCONV_OK:
         _raise(rc, "spconv_to_dense")
+    return out
+
+
+_BITS = {torch.uint32: 32, torch.int32: 32, torch.uint64: 64, torch.int64: 64}
+
+
+def _table_args(table_keys: torch.Tensor, table_values: torch.Tensor, keys: torch.Tensor):
+    if table_keys.dtype not in _BITS or table_values.dtype not in _BITS:
+        raise TypeError("table keys / values must be 32- or 64-bit integer tensors")
+    if keys.dtype != table_keys.dtype:
+        raise TypeError(f"keys dtype {keys.dtype} differs from the table's {table_keys.dtype}")
+    if not (table_keys.is_contiguous() and table_values.is_contiguous()):
+        raise ValueError("table tensors must be contiguous")
+    if table_keys.numel() != table_values.numel() or table_keys.numel() == 0:
+        raise ValueError("table keys and values must have the same, non-zero length")
+    return int(table_keys.numel()), _BITS[table_keys.dtype], _BITS[table_values.dtype]
+
+
+def hashmap_insert(table_keys: torch.Tensor, table_values: torch.Tensor, keys: torch.Tensor,
+                   values: torch.Tensor) -> None:
+    """hashmap_insert_cuda (hash.cu:8-71): insert keys -> values into the caller's table."""
+    lib = load_library()
+    dev = _require_cuda(table_keys, table_values, keys, values)
+    cap, kb, vb = _table_args(table_keys, table_values, keys)
+    if values.dtype != table_values.dtype or values.numel() != keys.numel():
+        raise ValueError("values must match the table's value dtype and the number of keys")
+    k, v = keys.contiguous(), values.contiguous()
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_hashmap_insert(table_keys.data_ptr(), table_values.data_ptr(), cap, kb, vb, k.data_ptr(),
+                                   v.data_ptr(), int(k.numel()), st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_hashmap_insert")
+    after_launch(dev)
+
+
+def hashmap_lookup(table_keys: torch.Tensor, table_values: torch.Tensor, keys: torch.Tensor) -> torch.Tensor:
+    """hashmap_lookup_cuda (hash.cu:73-146): values of keys (all ones if absent)."""
+    lib = load_library()
+    dev = _require_cuda(table_keys, table_values, keys)
+    cap, kb, vb = _table_args(table_keys, table_values, keys)
+    k = keys.contiguous()
+    out = torch.empty((k.numel(),), dtype=table_values.dtype, device=dev)
+    rc = lib.spconv_hashmap_lookup(table_keys.data_ptr(), table_values.data_ptr(), cap, kb, vb, k.data_ptr(),
+                                   out.data_ptr(), int(k.numel()), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_hashmap_lookup")
     return out
 
 
