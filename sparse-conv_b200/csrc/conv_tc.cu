@@ -185,9 +185,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     grid_dependency_wait();                  // the map build's order, masks and map
 
     // Tiles are taken from the end of the voxel order first: voxels with the most neighbours
-    // sort last, so the tiles with the most active offsets start earliest.
+    // sort last, so the tiles with the most active offsets start earliest. CTA c takes tiles
+    // c + kG (k >= 1) after a first tile G-1-c: the CTAs that get one tile fewer (the last
+    // round is partial) take the heaviest first tiles.
     const int G = gridDim.x;
     const int nt = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    auto tile_id = [&](int k) { return k == 0 ? G - 1 - (int)blockIdx.x : (int)blockIdx.x + k * G; };
     const bool use_masks = MWS > 0;
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
         return mbar_wait_or_abort(smem_u32(b), parity, s_abort);
@@ -202,7 +205,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             for (int j = 0; j < 4; ++j) {
                 r[j] = -1;
                 if (k < nt) {
-                    const int64_t p = (int64_t)(num_tiles - 1 - ((int)blockIdx.x + k * G)) * kTileM + 4 * lane + j;
+                    const int64_t p = (int64_t)(num_tiles - 1 - tile_id(k)) * kTileM + 4 * lane + j;
                     if (p < M) r[j] = order ? __ldg(order + p) : (int32_t)p;
                 }
             }
