@@ -220,6 +220,8 @@ def main():
     ap.add_argument("--no-backward", action="store_true", help="skip the training-step (forward + backward) figure")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run this many eager forwards of the workload and exit (a target for ncu)")
+    ap.add_argument("--profile-backward", action="store_true",
+                    help="with --profile-steps: each step is a forward + backward through autograd")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -251,8 +253,15 @@ def main():
         return sparse_submanifold_conv3d(feats, coords, shape, weight, algorithm=Algorithm.IMPLICIT_GEMM)
 
     if args.profile_steps > 0:
-        for _ in range(args.profile_steps):
-            step()
+        if args.profile_backward:
+            f_req = feats.detach().clone().requires_grad_(True)
+            w_req = weight.detach().clone().requires_grad_(True)
+            for _ in range(args.profile_steps):
+                o, _c = sparse_submanifold_conv3d(f_req, coords, shape, w_req, algorithm=Algorithm.IMPLICIT_GEMM)
+                o.backward(torch.ones_like(o))
+        else:
+            for _ in range(args.profile_steps):
+                step()
         torch.cuda.synchronize()
         _native.check_errors(dev)
         print("profile steps done:", args.workload, w.num_voxels, "voxels x", args.profile_steps)
