@@ -204,6 +204,20 @@ int spconv_submanifold_conv_forward_ex(
     const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
     void *out, int32_t *status, void *stream, int kernel_choice);
 
+/* Input gradient of the submanifold conv:
+ *   grad_in[j, ci] = sum_v sum_co grad_out[nbr_t[j, v], co] * weight_t[ci, v, co]
+ * with weight_t[ci, v, co] = weight[co, v, ci] and nbr_t the transposed map. For odd kernel
+ * volumes (every side odd, so the offsets are symmetric) nbr_t[j, v] = nbr[j, V-1-v]: the
+ * kernels read neighbor_map / masks with the offsets reversed and nbr_t / masks_t may be NULL.
+ * Even volumes need nbr_t / masks_t from spconv_transpose_neighbor_map. order: the map
+ * build's (any permutation). Replaces the EXPLICIT_GEMM input gradient of
+ * ops/submanifold_conv3d.py:117-127. */
+int spconv_submanifold_conv_backward_input(
+    const void *grad_out, int dtype, int64_t num_coords, int Co, const void *weight_t, int Ci,
+    int kernel_volume, const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
+    const int32_t *neighbor_map_t, const uint32_t *masks_t, void *grad_in,
+    int32_t *status, void *stream);
+
 /* Transposed kernel map for the input gradient: neighbor_map_t[j, v] = i where
  * neighbor_map[i, v] = j (at most one such i for distinct coordinates; the largest if the
  * coordinates repeat), -1 if none; masks_t (optional, [M, spconv_mask_words(V)]) its offset

@@ -14,7 +14,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 conv_simt_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
                  const T *__restrict__ bias, const int32_t *__restrict__ nbr,
-                 int64_t M, int Ci, int Co, int V, T *__restrict__ out) {
+                 int64_t M, int Ci, int Co, int V, int flip, T *__restrict__ out) {
     const int64_t total = M * (int64_t)Co;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
@@ -23,7 +23,7 @@ conv_simt_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
         const int32_t *nr = nbr + row * V;
         float acc = 0.0f;
         for (int v = 0; v < V; ++v) {
-            const int32_t n = __ldg(nr + v);
+            const int32_t n = __ldg(nr + (flip ? V - 1 - v : v));
             if (n < 0 || n >= M) continue;       // rows outside the feature table read as missing
             const T *f = feats + (int64_t)n * Ci;
             const T *w = weight + ((int64_t)co * V + v) * Ci;
@@ -67,17 +67,17 @@ int launch_conv_simt(const ConvArgs &a) {
         case SPCONV_F32:
             conv_simt_kernel<float><<<(int)blocks, 256, 0, a.stream>>>(
                 (const float *)a.feats, (const float *)a.weight, (const float *)a.bias, a.nbr,
-                a.M, a.Ci, a.Co, a.V, (float *)a.out);
+                a.M, a.Ci, a.Co, a.V, a.flip, (float *)a.out);
             break;
         case SPCONV_F16:
             conv_simt_kernel<__half><<<(int)blocks, 256, 0, a.stream>>>(
                 (const __half *)a.feats, (const __half *)a.weight, (const __half *)a.bias, a.nbr,
-                a.M, a.Ci, a.Co, a.V, (__half *)a.out);
+                a.M, a.Ci, a.Co, a.V, a.flip, (__half *)a.out);
             break;
         case SPCONV_BF16:
             conv_simt_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, a.stream>>>(
                 (const __nv_bfloat16 *)a.feats, (const __nv_bfloat16 *)a.weight,
-                (const __nv_bfloat16 *)a.bias, a.nbr, a.M, a.Ci, a.Co, a.V, (__nv_bfloat16 *)a.out);
+                (const __nv_bfloat16 *)a.bias, a.nbr, a.M, a.Ci, a.Co, a.V, a.flip, (__nv_bfloat16 *)a.out);
             break;
         default:
             set_error("unsupported dtype code %d", a.dtype);
@@ -132,6 +132,29 @@ static int launch_conv(const ConvArgs &a, int kernel_choice) {
         ((uintptr_t)weight & 15u) == 0 && ((uintptr_t)out & 15u) == 0)
         return launch_conv_tc(a);
     return launch_conv_simt(a);
+}
+
+extern "C" int spconv_submanifold_conv_backward_input(
+    const void *grad_out, int dtype, int64_t M, int Co, const void *weight_t, int Ci, int V,
+    const int32_t *nbr, const uint32_t *masks, const int32_t *order,
+    const int32_t *nbr_t, const uint32_t *masks_t, void *grad_in, int32_t *status, void *stream) {
+    SPCONV_REQUIRE(M >= 0 && M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld out of range", (long long)M);
+    SPCONV_REQUIRE(Ci > 0 && Co > 0, SPCONV_ERR_ARG, "channels must be positive (Ci=%d Co=%d)", Ci, Co);
+    SPCONV_REQUIRE(V > 0 && V <= 1024, SPCONV_ERR_ARG, "kernel volume %d out of range [1, 1024]", V);
+    SPCONV_REQUIRE(dtype == SPCONV_F32 || dtype == SPCONV_F16 || dtype == SPCONV_BF16,
+                   SPCONV_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (M == 0) return SPCONV_OK;
+    // Odd V <=> every kernel side odd <=> offsets symmetric: the transpose is the flip.
+    const bool flip = (V & 1) != 0;
+    SPCONV_REQUIRE(grad_out && weight_t && grad_in && (flip ? nbr != nullptr : nbr_t != nullptr), SPCONV_ERR_ARG,
+                   "null pointer argument (even kernel volumes need the transposed map)");
+    ConvArgs a{grad_out, dtype, M, Co, weight_t, nullptr, Ci, V, spconv_mask_words(V),
+               flip ? nbr : nbr_t, flip ? masks : masks_t, order, grad_in, status, (cudaStream_t)stream};
+    a.flip = flip ? 1 : 0;
+    stage_mark(SPCONV_STAGE_CONV, 0, a.stream);
+    const int rc = launch_conv(a, SPCONV_KERNEL_AUTO);
+    if (rc == SPCONV_OK) stage_mark(SPCONV_STAGE_CONV, 1, a.stream);
+    return rc;
 }
 
 extern "C" int spconv_submanifold_conv_forward(

@@ -22,6 +22,9 @@ struct ConvArgs {
     void *out;
     int32_t *status;
     cudaStream_t stream;
+    // 1: read the map with offsets reversed (column V-1-v for offset v) and the masks likewise:
+    // for odd kernel sizes that is the transposed map, so the input gradient needs no copy
+    int flip = 0;
 };
 
 bool tc_supported(int dtype, int Ci, int Co, int V);

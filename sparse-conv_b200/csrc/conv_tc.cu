@@ -126,7 +126,7 @@ __device__ __forceinline__ uint32_t sel4(uint32_t a, uint32_t b, uint32_t c, uin
     return w == 0 ? a : (w == 1 ? b : (w == 2 ? c : d));
 }
 
-template <int CI, int CO, typename T>
+template <int CI, int CO, typename T, bool FLIP>
 __global__ void __launch_bounds__(kTcThreads, TcCfg<CI, CO>::kMinBlocks)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__ feats,
                const T *__restrict__ bias, const int32_t *__restrict__ nbr,
@@ -263,8 +263,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 for (int w = 0; w < kMaxMaskWords; ++w) {
                     if (w < MWS) {
                         // active offsets in ascending order: lane b writes bit b of this word
-                        if ((tm[w] >> lane) & 1u)
-                            s_tact[base_v + __popc(tm[w] & ((1u << lane) - 1u))] = (uint8_t)(w * 32 + lane);
+                        // (FLIP: offset V-1-u for mask bit u, so the list is reversed)
+                        if ((tm[w] >> lane) & 1u) {
+                            const int pos = base_v + __popc(tm[w] & ((1u << lane) - 1u));
+                            if (FLIP) s_tact[nact - 1 - pos] = (uint8_t)(V - 1 - (w * 32 + lane));
+                            else s_tact[pos] = (uint8_t)(w * 32 + lane);
+                        }
                         base_v += __popc(tm[w]);
                     }
                 }
@@ -335,7 +339,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 int32_t *dn = &s_n[cb * Cfg::kBufWords + i];
                 // A row's map entry is -1 where its mask bit is clear, so no per-row mask test is
                 // needed: the lanes of one row fetch the same cache line(s) either way.
-                const int32_t *nv = nbr + v;
+                const int32_t *nv = nbr + (FLIP ? V - 1 - v : v);
                 auto load_index = [&](int r) {
                     const int32_t row = s_trow[t * kTileM + r];
                     int32_t *d = dn + r * kNPitch;
@@ -436,9 +440,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 const int v = s_act[cb * kActMax + i];
                 int32_t n[LPR];
                 if (Cfg::kRows && crows) {
+                    const int vc = FLIP ? V - 1 - v : v;      // the map column of offset v
 #pragma unroll
                     for (int q = 0; q < LPR; ++q)
-                        n[q] = rowp[q * kRowWindow + ((v + (int)(rotw[q >> 2] >> (8 * (q & 3)))) & 31)];
+                        n[q] = rowp[q * kRowWindow + ((vc + (int)(rotw[q >> 2] >> (8 * (q & 3)))) & 31)];
                 } else {
                     const int32_t *np = &s_n[cb * Cfg::kBufWords + row0 * kNPitch + i];
 #pragma unroll
@@ -626,10 +631,10 @@ static bool make_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t cols, uint6
     return true;
 }
 
-template <int CI, int CO, typename T>
-static int launch_tc(const ConvArgs &a) {
+template <int CI, int CO, typename T, bool FLIP>
+static int launch_tc_k(const ConvArgs &a) {
     using Cfg = TcCfg<CI, CO>;
-    auto kern = conv_tc_kernel<CI, CO, T>;
+    auto kern = conv_tc_kernel<CI, CO, T, FLIP>;
     const int MWS = (a.masks && a.MW <= kMaxMaskWords) ? a.MW : 0;
     // Shared memory is padded so that no more CTAs fit on an SM than its 512 TMEM columns
     // serve (228 KB of shared memory per SM, 1 KB reserved per CTA): tcgen05.alloc never waits.
@@ -667,6 +672,11 @@ static int launch_tc(const ConvArgs &a) {
                                       a.M, a.V, a.MW, MWS, num_tiles, row_mode, a.status);
     if (le != cudaSuccess) return check_launch("conv_tc_kernel launch");
     return check_launch("conv_tc_kernel");
+}
+
+template <int CI, int CO, typename T>
+static int launch_tc(const ConvArgs &a) {
+    return a.flip ? launch_tc_k<CI, CO, T, true>(a) : launch_tc_k<CI, CO, T, false>(a);
 }
 
 bool tc_supported(int dtype, int Ci, int Co, int V) {

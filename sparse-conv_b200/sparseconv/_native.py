@@ -66,6 +66,9 @@ SIGNATURES = {
         _c_void_p, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
     "spconv_hashmap_lookup": (_c_int, [
         _c_void_p, _c_void_p, _c_i64, _c_int, _c_int, _c_void_p, _c_void_p, _c_i64, _c_void_p]),
+    "spconv_submanifold_conv_backward_input": (_c_int, [
+        _c_void_p, _c_int, _c_i64, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_transpose_neighbor_map": (_c_int, [
         _c_void_p, _c_i64, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_weight_grad_workspace_bytes": (_c_i64, [_c_i64, _c_int]),
@@ -473,6 +476,46 @@ def hashmap_lookup(table_keys: torch.Tensor, table_values: torch.Tensor, keys: t
                                    out.data_ptr(), int(k.numel()), _stream_ptr(dev))
     if rc != SPCONV_OK:
         _raise(rc, "spconv_hashmap_lookup")
+    return out
+
+
+def conv_backward_input(grad_out: torch.Tensor, weight: torch.Tensor, nbr: torch.Tensor,
+                        masks: Optional[torch.Tensor], order: Optional[torch.Tensor],
+                        nbr_t: Optional[torch.Tensor] = None, masks_t: Optional[torch.Tensor] = None
+                        ) -> torch.Tensor:
+    """grad_in[j] = sum over (i, v) with nbr[i, v] = j of grad_out[i] @ weight[:, v, :], for
+    weight [Co, V, Ci] (or [Co, Kw, Kh, Kd, Ci]). Odd V reads ``nbr`` with the offsets reversed;
+    even V needs ``nbr_t`` / ``masks_t`` from ``transpose_neighbor_map``."""
+    lib = load_library()
+    dev = _require_cuda(grad_out, weight, nbr, masks, order, nbr_t, masks_t)
+    if grad_out.dtype not in DTYPE_CODES:
+        raise TypeError(f"unsupported dtype {grad_out.dtype}")
+    g = grad_out.contiguous()
+    M, Co = int(g.shape[0]), int(g.shape[1])
+    nb = nbr.view(torch.int32) if nbr.dtype == torch.uint32 else nbr
+    V = int(nb.shape[1])
+    Ci = int(weight.shape[-1])
+    if int(weight.shape[0]) != Co:
+        raise ValueError(f"weight has {weight.shape[0]} output channels, grad_out {Co}")
+    if V % 2 == 0 and nbr_t is None:
+        raise ValueError("an even kernel volume needs the transposed map (transpose_neighbor_map)")
+    w_t = weight.reshape(Co, V, Ci).permute(2, 1, 0).to(g.dtype).contiguous()      # [Ci, V, Co]
+
+    def i32(t):
+        return None if t is None else (t.view(torch.int32) if t.dtype == torch.uint32 else t)
+
+    def ptr(t):
+        return None if t is None else t.data_ptr()
+    out = torch.empty((M, Ci), dtype=g.dtype, device=dev)
+    if M == 0:
+        return out
+    before_launch(dev)
+    st = status_word(dev)
+    rc = lib.spconv_submanifold_conv_backward_input(
+        g.data_ptr(), DTYPE_CODES[g.dtype], M, Co, w_t.data_ptr(), Ci, V, nb.data_ptr(), ptr(i32(masks)),
+        ptr(order), ptr(i32(nbr_t)), ptr(i32(masks_t)), out.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
+    if rc != SPCONV_OK:
+        _raise(rc, "spconv_submanifold_conv_backward_input")
     return out
 
 

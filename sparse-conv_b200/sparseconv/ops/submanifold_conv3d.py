@@ -141,10 +141,11 @@ class SubMConv3dFunction(Function):
         """(grad_feats, grad_weight, grad_bias) of the conv (ops:105-150); every algorithm runs
         the CUDA kernels.
 
-        grad_feats is a forward conv of grad_output over the transposed map (cached on
-        ``neighbor_cache`` as ``neighbor_map_t`` / ``masks_t``) with the weight's channel axes
-        swapped. For odd kernel sizes the transposed map is the reference's flipped map
-        (ops:123-126); for even sizes it is the exact transpose, where the flip is not.
+        grad_feats is a forward conv of grad_output over the transposed map with the weight's
+        channel axes swapped. For odd kernel sizes the transposed map is the reference's
+        flipped map (ops:123-126) and the kernels read the forward map with the offsets
+        reversed; for even sizes it is built (the exact transpose, where the flip is not) and
+        cached on ``neighbor_cache`` as ``neighbor_map_t`` / ``masks_t``.
         grad_weight / grad_bias are accumulated in fp32 and returned in the parameters' dtypes.
         ``needs`` = which of (feats, weight, bias) want a gradient (default: requires_grad).
         """
@@ -159,13 +160,14 @@ class SubMConv3dFunction(Function):
         g = grad_output.to(feats.dtype).contiguous()
         grad_input = grad_weight = grad_bias = None
         if needs[0]:
-            nbr_t = getattr(neighbor_cache, "neighbor_map_t", None)
-            masks_t = getattr(neighbor_cache, "masks_t", None)
-            if nbr_t is None:
-                nbr_t, masks_t = _native.transpose_neighbor_map(nbr)
-                neighbor_cache.neighbor_map_t, neighbor_cache.masks_t = nbr_t, masks_t
-            w_t = weight.reshape(Co, V, Ci).permute(2, 1, 0).to(feats.dtype).contiguous()
-            grad_input = _native.conv_forward(g, w_t, None, nbr_t, masks_t, order)
+            nbr_t = masks_t = None
+            if V % 2 == 0:           # even sizes: the flipped map is not the transpose
+                nbr_t = getattr(neighbor_cache, "neighbor_map_t", None)
+                masks_t = getattr(neighbor_cache, "masks_t", None)
+                if nbr_t is None:
+                    nbr_t, masks_t = _native.transpose_neighbor_map(nbr)
+                    neighbor_cache.neighbor_map_t, neighbor_cache.masks_t = nbr_t, masks_t
+            grad_input = _native.conv_backward_input(g, weight, nbr, masks, order, nbr_t, masks_t)
         if needs[1] or (bias is not None and needs[2]):
             gw, gb = _native.conv_weight_grad(feats.contiguous(), g, nbr, order,
                                               with_bias=bias is not None and needs[2], masks=masks)

@@ -130,7 +130,7 @@ def test_autograd_only_the_requested_gradients():
     out, cache = sparse_submanifold_conv3d(f, c, torch.Size(shape), w, algorithm=Algorithm.IMPLICIT_GEMM)
     out.float().sum().backward()
     assert f.grad is None and w.grad is not None
-    assert getattr(cache, "neighbor_map_t", None) is None     # no input gradient: no transposed map
+    assert getattr(cache, "neighbor_map_t", None) is None     # odd kernel: never a transposed map
 
 
 @pytest.mark.parametrize("name", ["cube", "lidar"])
@@ -155,3 +155,22 @@ def test_full_size_backward(name):
     _close(wt.grad.float().cpu().numpy().reshape(Co, V, Ci), gw_ref, w_.dtype, "grad_weight")
     rows = np.sort(np.random.default_rng(0).choice(w_.num_voxels, size=4096, replace=False))
     _close(f.grad.float().cpu().numpy()[rows], gf_ref[rows], w_.dtype, "grad_feats")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("ci,co", [(32, 32), (64, 64), (16, 128), (3, 8)])
+@pytest.mark.parametrize("case", ["rand3", "dense3", "rand5", "dil2", "aniso", "even2", "k1"])
+def test_backward_input_flip_and_transpose(dtype, ci, co, case):
+    """The input gradient with the offsets reversed (odd kernel volumes) and over the built
+    transposed map (any volume) agree with the oracle, with and without masks / order."""
+    coords, shape, ks, dil = gpu_cases.small_cases()[case]
+    nbr, masks, order, f, w, go, (gf_ref, _gw, _gb) = _grads(ci + co, coords, shape, ks, dil, ci, co, dtype)
+    V = nbr.shape[1]
+    nbr_t, masks_t = _native.transpose_neighbor_map(nbr)
+    variants = [(masks, order, nbr_t, masks_t), (None, None, nbr_t, None)]
+    if V % 2 == 1:
+        variants += [(masks, order, None, None), (None, None, None, None)]
+    for mk, od, nt, mt in variants:
+        gf = _native.conv_backward_input(go.cuda(), w.cuda(), nbr, mk, od, nt, mt)
+        torch.cuda.synchronize()
+        _close(gf.float().cpu().numpy(), gf_ref, dtype, "grad_feats")
