@@ -217,6 +217,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--e2e-streams", type=int, default=2, help="CUDA streams the end-to-end steps rotate over")
     ap.add_argument("--no-backward", action="store_true", help="skip the training-step (forward + backward) figure")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run this many eager forwards of the workload and exit (a target for ncu)")
@@ -366,20 +367,23 @@ def main():
     e2e_serial_ms = shards.max_over_ranks(e0.elapsed_time(e1))
     e2e_serial = voxels_all * KE / (e2e_serial_ms / 1e3)
 
-    # The same steps pipelined over two CUDA streams, as a host feeding batches would run them:
+    # The same steps pipelined over CUDA streams (two by default: on the cube 548 M voxels/s vs
+    # 540 with three and 457 with four, against a 573 M ceiling of the two copy directions
+    # running together), as a host feeding batches would run them:
     # step i+1's host-to-device copies overlap step i's op and device-to-host copy (separate
     # copy engines). Every step still copies its own inputs in and its result out in the
     # timed region.
-    e2e_streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
-    outs_h = [out_h, torch.empty_like(out_h).pin_memory()]
+    NS = max(2, args.e2e_streams)
+    e2e_streams = [torch.cuda.Stream(dev) for _ in range(NS)]
+    outs_h = [out_h] + [torch.empty_like(out_h).pin_memory() for _ in range(NS - 1)]
 
     def e2e_step_on(j):
-        s = e2e_streams[j % 2]
+        s = e2e_streams[j % NS]
         with torch.cuda.stream(s):
             c_d = coords_h.to(dev, non_blocking=True)
             f_d = feats_h.to(dev, non_blocking=True)
             o, _c = sparse_submanifold_conv3d(f_d, c_d, shape, weight, algorithm=Algorithm.IMPLICIT_GEMM)
-            outs_h[j % 2].copy_(o, non_blocking=True)
+            outs_h[j % NS].copy_(o, non_blocking=True)
 
     for j in range(max(args.warmup, 2)):
         e2e_step_on(j)
@@ -465,7 +469,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": int(coords_h.numel() * 4 + feats_h.numel() * feats_h.element_size()),
                     "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()), "steps": KE,
-                    "pipelined": "two CUDA streams: step i+1's H2D overlaps step i's op and D2H",
+                    "pipelined": f"{NS} CUDA streams: step i+1's H2D overlaps step i's op and D2H",
                     "serial_value": e2e_serial},
             "gpu_launches": _launches_per_step(w.num_voxels, int(np.prod(w.kernel_size))) * K,
             "clocks": clk,
