@@ -523,7 +523,7 @@ constexpr int kMapK3Threads = 256;
 constexpr int kK3Batch = 4;
 
 template <bool BITMAP>
-__global__ void __launch_bounds__(kMapK3Threads, 3)
+__global__ void __launch_bounds__(kMapK3Threads, 4)
 map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
