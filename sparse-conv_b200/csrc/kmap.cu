@@ -668,10 +668,14 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
 //     (e.g. 5x5x5), with the occupancy bitmap: the same two phases as 2c with the kernel
 //     shape at run time. Phase 1 reads one funnel-shifted bitmap window per (dx, dy) column
 //     (four columns' loads in flight) and keeps the in-range z cells of it; phase 2 probes
-//     the candidates, four at a time. Rows are staged in shared memory pre-filled with -1.
+//     the candidates, four at a time, 32 offset columns at a time: the chunk's row segments
+//     are staged in shared memory pre-filled with -1 and written a warp per row segment,
+//     which keeps the stage at 16.5 KB whatever V is (six blocks per SM instead of two).
 // ---------------------------------------------------------------------------------------
 constexpr int kMapColsThreads = 128;
 constexpr int kMapColsMaxV = 128;
+constexpr int kMapColsStride = 33;
+constexpr int kMapColsMinBlocks = 6;
 
 __device__ __forceinline__ void or_word4(uint32_t (&m)[4], int w, uint32_t x) {
     if (w == 0) m[0] |= x;
@@ -695,21 +699,24 @@ __device__ __forceinline__ int pop_lowest4(uint32_t (&m)[4]) {
     return -1;
 }
 
-__global__ void __launch_bounds__(kMapColsThreads)
+__device__ __forceinline__ uint32_t get_word4(const uint32_t (&m)[4], int w) {
+    return w == 0 ? m[0] : w == 1 ? m[1] : w == 2 ? m[2] : m[3];
+}
+
+__global__ void __launch_bounds__(kMapColsThreads, kMapColsMinBlocks)
 map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Kw, int Kh, int Kd,
                 int Dw, int Dh, int Dd, int V, int MW, const unsigned long long *__restrict__ table,
                 const uint32_t *__restrict__ bitmap, int64_t bm_words, uint64_t gmask, uint32_t shift,
                 int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
-    extern __shared__ int4 s_stage4[];                           // [kMapColsThreads * V] int32, padded to 16 B
-    int32_t *s_stage = reinterpret_cast<int32_t *>(s_stage4);
+    // 32 offset columns of every row of the block; stride 33 keeps both the per-thread
+    // row writes and the per-warp row-segment reads free of bank conflicts.
+    __shared__ int32_t s_stage[kMapColsThreads * kMapColsStride];
 
     const int tid = threadIdx.x;
     const int64_t i0 = (int64_t)blockIdx.x * kMapColsThreads;
     const int nvox = (M - i0) < (int64_t)kMapColsThreads ? (int)(M - i0) : kMapColsThreads;
-    const int stage_words = kMapColsThreads * V;
     for (int j = tid; j < kOrderBuckets; j += kMapColsThreads) s_hist[j] = 0u;
-    for (int j = tid; j < (stage_words + 3) / 4; j += kMapColsThreads) s_stage4[j] = make_int4(-1, -1, -1, -1);
 
     const bool valid = tid < nvox;
     const int64_t i = i0 + tid;
@@ -775,44 +782,64 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     const int vc = V / 2;                                       // the centre entry is the voxel itself
     clear_bit4(cand, vc);
 
-    __syncthreads();                                            // hist zeroed, stage pre-filled
+    // Phase 2, one 32-column chunk of the rows at a time: probe the chunk's candidates
+    // (kK3Batch in flight), then the block writes the chunk's row segments, a warp per row.
     uint32_t bits[4] = {0u, 0u, 0u, 0u};
-    if (valid) {
-        s_stage[tid * V + vc] = (int32_t)i;
-        or_word4(bits, vc >> 5, 1u << (vc & 31));
-    }
-
-    // Phase 2: probe candidate offsets, kK3Batch in flight.
     bool wrapped = false;
-    while (cand[0] | cand[1] | cand[2] | cand[3]) {
-        int vv[kK3Batch];
-        uint32_t key[kK3Batch];
-        uint64_t grp[kK3Batch];
-        unsigned long long word[kK3Batch][kGroup];
-#pragma unroll
-        for (int b = 0; b < kK3Batch; ++b) {
-            const int v = pop_lowest4(cand);
-            vv[b] = v;
-            if (v >= 0) {
-                const int cx = v / (Kh * Kd), rem = v - cx * (Kh * Kd);
-                const int cy = rem / Kd, cz = rem - cy * Kd;
-                const int64_t kn = key_c + (int64_t)(cx - rw) * Dw * HD + (int64_t)(cy - rh) * Dh * D + (cz - rd) * Dd;
-                key[b] = (uint32_t)kn;
-                grp[b] = home32(key[b], shift);
-                load_group(table, grp[b], word[b]);
-            }
+    int32_t *row = s_stage + tid * kMapColsStride;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nch = (V + 31) >> 5;
+    for (int ch = 0; ch < nch; ++ch) {
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) row[j] = -1;
+        uint32_t got = 0u;
+        if (valid && (vc >> 5) == ch) {
+            row[vc & 31] = (int32_t)i;
+            got = 1u << (vc & 31);
         }
+        uint32_t cw = valid ? get_word4(cand, ch) : 0u;
+        while (cw) {
+            int vv[kK3Batch];
+            uint32_t key[kK3Batch];
+            uint64_t grp[kK3Batch];
+            unsigned long long word[kK3Batch][kGroup];
 #pragma unroll
-        for (int b = 0; b < kK3Batch; ++b) {
-            if (vv[b] >= 0) {
-                int32_t r = table_resolve<false>(table, nullptr, gmask, key[b], grp[b], word[b]);
-                if (r == -2) { wrapped = true; r = -1; }
-                if (r >= 0) {
-                    s_stage[tid * V + vv[b]] = r;
-                    or_word4(bits, vv[b] >> 5, 1u << (vv[b] & 31));
+            for (int b = 0; b < kK3Batch; ++b) {
+                vv[b] = -1;
+                if (cw) {
+                    const int bl = __ffs(cw) - 1;
+                    cw &= cw - 1u;
+                    const int v = (ch << 5) + bl;
+                    vv[b] = bl;
+                    const int cx = v / (Kh * Kd), rem = v - cx * (Kh * Kd);
+                    const int cy = rem / Kd, cz = rem - cy * Kd;
+                    const int64_t kn = key_c + (int64_t)(cx - rw) * Dw * HD + (int64_t)(cy - rh) * Dh * D + (cz - rd) * Dd;
+                    key[b] = (uint32_t)kn;
+                    grp[b] = home32(key[b], shift);
+                    load_group(table, grp[b], word[b]);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < kK3Batch; ++b) {
+                if (vv[b] >= 0) {
+                    int32_t r = table_resolve<false>(table, nullptr, gmask, key[b], grp[b], word[b]);
+                    if (r == -2) { wrapped = true; r = -1; }
+                    if (r >= 0) {
+                        row[vv[b]] = r;
+                        got |= 1u << vv[b];
+                    }
                 }
             }
         }
+        or_word4(bits, ch, got);
+        __syncthreads();                                        // the chunk's rows are staged
+        const int col = (ch << 5) + lane;
+        if (col < V) {
+            int32_t *out = nbr + i0 * (int64_t)V + col;
+            for (int r = warp; r < nvox; r += kMapColsThreads / 32)
+                out[(int64_t)r * V] = s_stage[r * kMapColsStride + lane];
+        }
+        __syncthreads();                                        // the stage is free again
     }
     if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
     {
@@ -831,19 +858,6 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
         if (valid && hist) aggregated_inc(s_hist, k, active);
     }
     __syncthreads();
-    {
-        // The block's rows form one contiguous range of the map.
-        int32_t *out = nbr + i0 * (int64_t)V;
-        const int total = nvox * V;
-        if (((uintptr_t)out & 15u) == 0) {
-            const int n4 = total >> 2;
-            int4 *dst = reinterpret_cast<int4 *>(out);
-            for (int e = tid; e < n4; e += kMapColsThreads) dst[e] = s_stage4[e];
-            for (int e = (n4 << 2) + tid; e < total; e += kMapColsThreads) out[e] = s_stage[e];
-        } else {
-            for (int e = tid; e < total; e += kMapColsThreads) out[e] = s_stage[e];
-        }
-    }
     if (hist) block_hist_flush(s_hist, hist);
 }
 
@@ -1204,15 +1218,9 @@ extern "C" int spconv_build_submanifold_neighbor_map(
                    (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
                    status);
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
-        const size_t smem = ((size_t)kMapColsThreads * V * sizeof(int32_t) + 15) / 16 * 16;
-        static bool cols_attr_done = false;
-        if (!cols_attr_done) {
-            cudaFuncSetAttribute(map_kernel_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-            cols_attr_done = true;
-        }
         const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
-        launch_pdl(map_kernel_cols, dim3(grid), dim3(kMapColsThreads), smem, stream,
+        launch_pdl(map_kernel_cols, dim3(grid), dim3(kMapColsThreads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW,
                    (const unsigned long long *)table, (const uint32_t *)bitmap, L.bitmap_words, gmask,
                    shift, neighbor_map, masks, hist, status);
