@@ -713,18 +713,37 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     // row writes and the per-warp row-segment reads free of bank conflicts.
     __shared__ int32_t s_stage[kMapColsThreads * kMapColsStride];
 
+    // Block-invariant offset tables: the key offset of every kernel offset v, and per (dx, dy)
+    // column its key offset and its x / y displacement (no divisions in the per-voxel loops).
+    __shared__ long long s_voff[kMapColsMaxV];
+    __shared__ int4 s_col[kMapColsMaxV];                       // {key offset lo, hi, dx, dy}
+
     const int tid = threadIdx.x;
     const int64_t i0 = (int64_t)blockIdx.x * kMapColsThreads;
     const int nvox = (M - i0) < (int64_t)kMapColsThreads ? (int)(M - i0) : kMapColsThreads;
     for (int j = tid; j < kOrderBuckets; j += kMapColsThreads) s_hist[j] = 0u;
+    {
+        const int64_t sxw = (int64_t)Dw * H * D, syw = (int64_t)Dh * D;
+        const int rw0 = Kw / 2, rh0 = Kh / 2, rd0 = Kd / 2;
+        if (tid < V) {                                          // V <= kMapColsThreads
+            const int cx = tid / (Kh * Kd), rem = tid - cx * (Kh * Kd);
+            const int cy = rem / Kd, cz = rem - cy * Kd;
+            s_voff[tid] = (cx - rw0) * sxw + (cy - rh0) * syw + (int64_t)(cz - rd0) * Dd;
+        }
+        if (tid < Kw * Kh) {
+            const int cx = tid / Kh, cy = tid - cx * Kh;
+            const int64_t dk = (cx - rw0) * sxw + (cy - rh0) * syw;
+            s_col[tid] = make_int4((int)(uint32_t)dk, (int)(dk >> 32), (cx - rw0) * Dw, (cy - rh0) * Dh);
+        }
+    }
+    __syncthreads();
 
     const bool valid = tid < nvox;
     const int64_t i = i0 + tid;
     int4 c = make_int4(0, 0, 0, 0);
     if (valid) c = __ldg(coords + i);
-    const int64_t HD = (int64_t)H * D;
     const int64_t key_c = (((int64_t)c.x * W + c.y) * H + c.z) * D + c.w;
-    const int rw = Kw / 2, rh = Kh / 2, rd = Kd / 2;
+    const int rd = Kd / 2;
     const int zlo = max(c.w - rd * Dd, 0);                      // window starts at the lowest in-range cell
     // in-range z cells of a column and their bit positions in the window
     uint32_t zsel = 0;
@@ -749,6 +768,7 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     uint32_t cand[4] = {0u, 0u, 0u, 0u};
     const int ncol = Kw * Kh;
     if (valid) {
+        const int64_t kz = key_c + (zlo - c.w);                 // key of the window start, centre column
         for (int q0 = 0; q0 < ncol; q0 += 4) {
             uint32_t lo[4], hi[4];
             int64_t kb[4];
@@ -756,13 +776,16 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int q = q0 + u;
-                const int cx = q / Kh, cy = q - (q / Kh) * Kh;
-                const int x = c.y + (cx - rw) * Dw, y = c.z + (cy - rh) * Dh;
-                in[u] = q < ncol && x >= 0 && x < W && y >= 0 && y < H;
+                in[u] = false;
                 lo[u] = hi[u] = 0u;
                 kb[u] = 0;
+                if (q < ncol) {
+                    const int4 e = s_col[q];
+                    const int x = c.y + e.z, y = c.z + e.w;
+                    in[u] = (unsigned)x < (unsigned)W && (unsigned)y < (unsigned)H;
+                    kb[u] = kz + (int64_t)(((uint64_t)(uint32_t)e.y << 32) | (uint32_t)e.x);
+                }
                 if (in[u]) {
-                    kb[u] = key_c + (int64_t)(cx - rw) * Dw * HD + (int64_t)(cy - rh) * Dh * D + (zlo - c.w);
                     const int64_t wi = kb[u] >> 5;
                     lo[u] = __ldg(bitmap + wi);
                     hi[u] = __ldg(bitmap + (wi + 1 < bm_words ? wi + 1 : wi));
@@ -811,9 +834,7 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
                     cw &= cw - 1u;
                     const int v = (ch << 5) + bl;
                     vv[b] = bl;
-                    const int cx = v / (Kh * Kd), rem = v - cx * (Kh * Kd);
-                    const int cy = rem / Kd, cz = rem - cy * Kd;
-                    const int64_t kn = key_c + (int64_t)(cx - rw) * Dw * HD + (int64_t)(cy - rh) * Dh * D + (cz - rd) * Dd;
+                    const int64_t kn = key_c + s_voff[v];
                     key[b] = (uint32_t)kn;
                     grp[b] = home32(key[b], shift);
                     load_group(table, grp[b], word[b]);
