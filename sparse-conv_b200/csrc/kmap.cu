@@ -223,16 +223,36 @@ insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, i
               unsigned long long *table, uint32_t *vals, uint32_t *bitmap, uint64_t gmask,
               uint32_t shift, int32_t *status) {
     grid_launch_dependents();                                   // the map kernel's setup overlaps this
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int4 c = __ldg(coords + i);
-        if (c.x < 0 || c.x >= N || c.y < 0 || c.y >= W || c.z < 0 || c.z >= H || c.w < 0 || c.w >= D) {
+    const int lane = threadIdx.x & 31;
+    // Whole warps iterate together (the bitmap update below shuffles across the warp).
+    for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < M;
+         w0 += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = w0 + lane;
+        bool ok = i < M;
+        int4 c = make_int4(0, 0, 0, 0);
+        if (ok) c = __ldg(coords + i);
+        if (ok && (c.x < 0 || c.x >= N || c.y < 0 || c.y >= W || c.z < 0 || c.z >= H || c.w < 0 || c.w >= D)) {
             raise_status(status, SPCONV_STATUS_COORD_RANGE);
-            continue;
+            ok = false;
         }
         const uint64_t flat = ((((uint64_t)c.x * W + c.y) * H + c.z) * D) + c.w;
-        if (bitmap) atomicOr(bitmap + (flat >> 5), 1u << (flat & 31));
-        if (!table_insert<KEY64>(table, vals, gmask, shift, flat, (uint32_t)i, status))
+        if (bitmap) {
+            // Voxels next to each other in z, adjacent in sorted input, share a bitmap word:
+            // each run of lanes with the same word ORs its bits together (segmented doubling
+            // over consecutive lanes) and the run's first lane sets them with one atomic.
+            // Words are < 2^25 (the bitmap covers at most 2^30 cells), so ~0 marks no voxel.
+            const uint32_t wi = ok ? (uint32_t)(flat >> 5) : 0xffffffffu;
+            uint32_t bits = ok ? 1u << (flat & 31) : 0u;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const uint32_t ob = __shfl_down_sync(0xffffffffu, bits, d);
+                const uint32_t ow = __shfl_down_sync(0xffffffffu, wi, d);
+                if (ow == wi) bits |= ob;
+            }
+            const uint32_t pw = __shfl_up_sync(0xffffffffu, wi, 1);
+            if (ok && (lane == 0 || pw != wi)) atomicOr(bitmap + wi, bits);
+        }
+        if (ok && !table_insert<KEY64>(table, vals, gmask, shift, flat, (uint32_t)i, status))
             raise_status(status, SPCONV_STATUS_TABLE_FULL);
     }
 }
