@@ -39,8 +39,8 @@ constexpr int kOrderPerThread = 2;     // voxels per thread in order_kernel
 // Radix-sort order (kernels of at most kSortMaxV offsets, at least kSortMinVoxels voxels):
 // tiles of kSortTile voxels, 8-bit digits, keys of at most 31 bits.
 constexpr int kSortThreads = 512;
-constexpr int kSortWarpItems = 256;                                  // 8 rounds of 32 per warp
-constexpr int kSortTile = (kSortThreads / 32) * kSortWarpItems;      // 4096
+constexpr int kSortWarpItems = 128;                                  // 4 rounds of 32 per warp
+constexpr int kSortTile = (kSortThreads / 32) * kSortWarpItems;      // 2048 (4096 left SMs idle)
 constexpr int kSortMaxPasses = 4;
 constexpr int kSortMaxV = 27;
 constexpr int64_t kSortMinVoxels = 1 << 19;
@@ -983,7 +983,7 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, const uint32
 //     share their high offsets, so a 128-voxel tile of the order needs few offsets beyond its
 //     voxels' own. Equal keys keep input order (the (b,x,y,z) order of the coordinates), so
 //     their feature rows are gathered with spatial locality.
-//     Per 8-bit digit pass: sort_count_kernel counts each 4096-key tile's digits,
+//     Per 8-bit digit pass: sort_count_kernel counts each 2048-key tile's digits,
 //     sort_scan_kernel (one block per digit) scans the counts over tiles, and
 //     sort_scatter_kernel ranks each tile's keys stably (lanes with equal digits found by
 //     eight ballots, per-warp digit counters, warps in input order) and writes them to their
