@@ -83,6 +83,24 @@ static int64_t bitmap_words_for(int batch, int W, int H, int D) {
     return (int64_t)((vol + 31.0L) / 32.0L);
 }
 
+// Lets a map kernel use up to 160 KB of dynamic shared memory. The attribute belongs to the
+// device's context, so it is set once per device and kernel (`slot` names the kernel).
+static void raise_smem_limit(const void *fn, int slot) {
+    constexpr int kDevs = 64, kSlots = 5;
+    static std::mutex mu;
+    static bool done[kDevs][kSlots] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevs || slot < 0 || slot >= kSlots) {
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        return;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev][slot]) {
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        done[dev][slot] = true;
+    }
+}
+
 static bool volume_fits_32(int batch, int W, int H, int D) {
     const long double vol = (long double)batch * W * H * D;
     return vol < 4294967296.0L;
@@ -1272,11 +1290,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         if ((size_t)nthr * vstride * 4 > (size_t)kMapStageMaxBytes) vstride = 0;
         const size_t smem = (size_t)nthr * (size_t)vstride * sizeof(int32_t);
         auto bm_fn = Kd <= 4 ? map_kernel_bm<4> : map_kernel_bm<kColBatchMax>;
-        static bool bm_attr_done[2] = {false, false};
-        if (!bm_attr_done[Kd <= 4 ? 0 : 1]) {
-            cudaFuncSetAttribute(bm_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-            bm_attr_done[Kd <= 4 ? 0 : 1] = true;
-        }
+        raise_smem_limit((const void *)bm_fn, Kd <= 4 ? 0 : 1);
         const int grid = (int)((M + nthr - 1) / nthr);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         bm_fn<<<grid, nthr, smem, stream>>>(
@@ -1291,12 +1305,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         const size_t map_smem = (size_t)V * (sizeof(int4) + sizeof(long long)) +
                                 (size_t)kMapThreads * (size_t)vstride * sizeof(int32_t);
         auto map_fn = key64 ? map_kernel<true, false> : (bitmap ? map_kernel<false, true> : map_kernel<false, false>);
-        static bool map_attr_done[3] = {false, false, false};
-        const int variant = key64 ? 0 : (bitmap ? 2 : 1);
-        if (map_smem > 48 * 1024 && !map_attr_done[variant]) {
-            cudaFuncSetAttribute(map_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-            map_attr_done[variant] = true;
-        }
+        if (map_smem > 48 * 1024) raise_smem_limit((const void *)map_fn, 2 + (key64 ? 0 : (bitmap ? 2 : 1)));
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         map_fn<<<map_grid, kMapThreads, map_smem, stream>>>(
             (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, bitmap,
