@@ -19,6 +19,7 @@
 // mma.sync fragments (A = grad_out^T, B = feats^T, K = voxels). Tiles whose voxels have no
 // neighbour at any of the group's offsets are skipped. Fp32 accumulators are added to the
 // fp32 gradient once per CTA. wgrad_simt_kernel covers fp32 and other channel counts.
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -458,14 +459,27 @@ static int launch_wgrad_mma(const void *feats, const void *gout, const int32_t *
                             const int32_t *order, int64_t M, int V, float *gw, void *scratch, cudaStream_t stream) {
     using Cfg = WgCfg<T, CO, CI>;
     auto kern = wgrad_mma_kernel<T, CO, CI>;
+    // Kernel attributes and occupancy belong to the device: computed once per device, under a
+    // lock so that concurrent host threads see them complete.
+    static std::mutex attr_mu;
     static bool attr_done[64] = {false};
+    static int occ_cache[64] = {0};
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
-            return check_launch("wgrad: set max dynamic shared memory");
-        attr_done[dev] = true;
+    int occ_dev = 1;
+    {
+        std::lock_guard<std::mutex> lock(attr_mu);
+        if (!attr_done[dev]) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
+                return check_launch("wgrad: set max dynamic shared memory");
+            int occ = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, Cfg::kThreads, Cfg::kSmem) != cudaSuccess || occ < 1)
+                occ = 1;
+            occ_cache[dev] = occ;
+            attr_done[dev] = true;
+        }
+        occ_dev = occ_cache[dev];
     }
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int num_tiles = (int)((M + kWgTile - 1) / kWgTile);
@@ -478,14 +492,7 @@ static int launch_wgrad_mma(const void *feats, const void *gout, const int32_t *
     if (int rc = check_launch("tile_union_kernel")) return rc;
     group_tiles_kernel<<<groups, 512, 0, stream>>>(uni, num_tiles, MW, V, Cfg::OG, list, cnt);
     if (int rc = check_launch("group_tiles_kernel")) return rc;
-    static int occ_cache[64] = {0};
-    if (occ_cache[dev] == 0) {
-        int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, Cfg::kThreads, Cfg::kSmem) != cudaSuccess || occ < 1)
-            occ = 1;
-        occ_cache[dev] = occ;
-    }
-    kern<<<sms * occ_cache[dev], Cfg::kThreads, Cfg::kSmem, stream>>>(
+    kern<<<sms * occ_dev, Cfg::kThreads, Cfg::kSmem, stream>>>(
         (const T *)feats, (const T *)gout, nbr, order, list, cnt, uni, MW, M, V, num_tiles, groups, gw);
     return check_launch("wgrad_mma_kernel");
 }

@@ -640,11 +640,15 @@ static int launch_tc_k(const ConvArgs &a) {
     // serve (228 KB of shared memory per SM, 1 KB reserved per CTA): tcgen05.alloc never waits.
     constexpr int kSmemForTmem = (228 * 1024) / (Cfg::kMaxCtasByTmem + 1);
     constexpr int smem = Cfg::kSmemBytes > kSmemForTmem ? Cfg::kSmemBytes : kSmemForTmem;
+    // Kernel attributes belong to the device's context: set once per device, under a lock
+    // so that concurrent host threads see them complete.
+    static std::mutex attr_mu;
     static bool attr_done[64] = {false};
     static int occ_cache[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
+    std::unique_lock<std::mutex> attr_lock(attr_mu);
     if (!attr_done[dev]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_launch("conv_tc: set max dynamic shared memory");
@@ -656,13 +660,15 @@ static int launch_tc_k(const ConvArgs &a) {
         occ_cache[dev] = occ < 1 ? 1 : occ;
         attr_done[dev] = true;
     }
+    const int occ_dev = occ_cache[dev];
+    attr_lock.unlock();
     CUtensorMap tw;
     if (!make_tmap_2d(&tw, a.weight, (uint64_t)a.V * CI, (uint64_t)CO, (uint64_t)a.V * CI * 2, Cfg::KC, CO))
         return SPCONV_ERR_CUDA;
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int num_tiles = (int)((a.M + kTileM - 1) / kTileM);
-    int grid = sms * occ_cache[dev];
+    int grid = sms * occ_dev;
     if (grid > num_tiles) grid = num_tiles;
     if (grid < 1) grid = 1;
     // Whole index rows are staged when one fits a 128-byte window and the map is 16-byte aligned.
