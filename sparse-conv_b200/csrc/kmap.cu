@@ -645,6 +645,33 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     uint32_t bits = valid ? (1u << (V / 2)) : 0u;
     if (valid) s_stage[tid * V + V / 2] = (int32_t)i;
 
+    // Sorted input keeps a voxel's z - Dd and z + Dd neighbours in the adjacent rows. With
+    // unique coordinates (the insert found no duplicate) a row holding that coordinate is the
+    // neighbour, so those offsets need no probe; otherwise they are probed as usual.
+    if (valid && (cand & ((1u << (V / 2 - 1)) | (1u << (V / 2 + 1)))) && status != nullptr &&
+        (*reinterpret_cast<volatile int32_t *>(status) & SPCONV_STATUS_DUPLICATE) == 0) {
+        if ((cand >> (V / 2 + 1)) & 1u) {
+            if (i + 1 < M) {
+                const int4 n = __ldg(coords + i + 1);
+                if (n.x == c.x && n.y == c.y && n.z == c.z && n.w == c.w + Dd) {
+                    s_stage[tid * V + V / 2 + 1] = (int32_t)(i + 1);
+                    bits |= 1u << (V / 2 + 1);
+                    cand &= ~(1u << (V / 2 + 1));
+                }
+            }
+        }
+        if ((cand >> (V / 2 - 1)) & 1u) {
+            if (i > 0) {
+                const int4 n = __ldg(coords + i - 1);
+                if (n.x == c.x && n.y == c.y && n.z == c.z && n.w == c.w - Dd) {
+                    s_stage[tid * V + V / 2 - 1] = (int32_t)(i - 1);
+                    bits |= 1u << (V / 2 - 1);
+                    cand &= ~(1u << (V / 2 - 1));
+                }
+            }
+        }
+    }
+
     // Phase 2: probe candidate offsets, kK3Batch in flight.
     bool wrapped = false;
     while (cand) {
