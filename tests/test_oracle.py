@@ -133,3 +133,22 @@ def test_reference_map_fixtures():
         ks, dil = d[f"{name}__kernel"], d[f"{name}__dilation"]
         np.testing.assert_array_equal(oracle.neighbor_map(coords, shape, ks, dil),
                                       d[f"{name}__map"], err_msg=name)
+
+
+@pytest.mark.parametrize("dil", [(1, 1, 1), (1, 1, 2)])
+def test_adjacent_rows_are_z_neighbours_of_sorted_unique_coords(dil):
+    """The 3x3x3 map kernel takes offsets V/2 - 1 and V/2 + 1 (z - d, z + d) from the adjacent
+    input rows when those rows hold exactly that coordinate and no coordinate repeats. For
+    unique coordinates that is the reference's answer: check it on the oracle's maps."""
+    rng = np.random.default_rng(3)
+    shape = (2, 1, 12, 10, 40)
+    cells = np.stack(np.meshgrid(np.arange(2), np.arange(12), np.arange(10), np.arange(40), indexing="ij"), -1)
+    cells = cells.reshape(-1, 4)
+    coords = cells[rng.random(len(cells)) < 0.35].astype(np.int32)   # sorted (b, x, y, z), unique
+    nbr = oracle.neighbor_map(coords, shape, (3, 3, 3), dil).view(np.int32)
+    V, d = 27, dil[2]
+    up = np.nonzero(np.all(coords[1:] == coords[:-1] + np.array([0, 0, 0, d]), axis=1))[0]
+    down = np.nonzero(np.all(coords[:-1] == coords[1:] - np.array([0, 0, 0, d]), axis=1))[0] + 1
+    assert len(up) > 100 and len(down) > 100
+    np.testing.assert_array_equal(nbr[up, V // 2 + 1], up + 1)
+    np.testing.assert_array_equal(nbr[down, V // 2 - 1], down - 1)
