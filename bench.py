@@ -4,13 +4,16 @@
 
 One step = ``sparse_submanifold_conv3d(feats, coords, shape, weight, IMPLICIT_GEMM)`` on one
 batch with no cached map: hash-table build, kernel map, voxel order and conv. The default
-workload is the random-occupancy cube (B=4, 128^3, p=0.02, C=32 -> 32, 3^3, fp16); other
-workloads (``indoor``, ``lidar``, ``wide3``, ``wide5``, ``toy``) run with ``--workload``.
+workload is the indoor-surface scene (B=8, 512^3, 20 planes + 30 spheres per sample, 2.0 M
+voxels, C=64 -> 64, 3^3, bf16), the largest single-GPU workload; others (``cube``, ``lidar``,
+``wide3``, ``wide5``, ``toy``) run with ``--workload``.
 
-Metric: voxels/s over all ranks (plus effective TFLOP/s in ``effective``). Under torchrun
-each rank runs its own batch of the same shape (seed = rank): weak scaling, no collective
-on the data path; the step time is the max over ranks of the summed per-step CUDA-event
-durations. The timed steps are replays of a CUDA graph holding one complete forward (no
+Metric: voxels/s over all ranks (plus effective TFLOP/s in ``effective``). Under torchrun the
+default ``--shard batch`` splits the workload's own batch over the ranks (rank r takes the
+samples b with b % N == r, renumbered locally; strong scaling: the total work is fixed), with
+no collective on the data path; ``--shard replica`` gives every rank its own full batch of the
+same shape (seed = rank; weak scaling). The step time is the max over ranks of the summed
+per-step CUDA-event durations. The timed steps are replays of a CUDA graph holding one complete forward (no
 cached map), so host-side Python does not sit between kernels; the eager API time per step is
 reported beside it. The L2 (126 MB) is flushed by a 256 MB write between timed steps, outside
 the step events. Per-kernel times (``stages_ms_per_step``, ``roofline``) come from the
@@ -23,8 +26,12 @@ pipelined over two CUDA streams (step i+1's H2D overlaps step i's op and D2H, as
 batches would run them); ``e2e.serial_value`` is the same with every step on one stream.
 
 ``--impl reference`` times the reference's CPU path on this host instead: the oracle's C
-restatement of the reference map builder (OpenMP, all cores) plus the reference's
-EXPLICIT_GEMM forward restated on CPU torch in fp32 (all threads); rank 0 only.
+restatement of the reference map builder (OpenMP, all cores, every voxel) plus the reference's
+EXPLICIT_GEMM forward restated on CPU torch in fp32 (all threads) over a row sample of the map
+(at most 2^27 im2col elements), scaled to the whole workload; rank 0 only. The same line
+carries ``reference_gpu``: the reference's own GPU forward (its CUDA map builder compiled from
+its sources + its Triton implicit GEMM, through its public ``sparse_submanifold_conv3d``) timed
+on cuda:0 by ``oracle/ref_gpu.py`` in a separate process.
 """
 from __future__ import annotations
 
@@ -148,65 +155,112 @@ def _alg_figures(w, nnz: int):
                 map_bytes=map_bytes, insert_bytes=insert_bytes, order_bytes=order_bytes)
 
 
+def _config(w) -> dict:
+    """The workload's description; both arms print exactly this dict as ``config``."""
+    return dict(w.describe(), l2="GPU arm: flushed between timed steps (256 MB write)")
+
+
+def _cpu_sampler(w):
+    """One CPU step of the reference's path on the host's cores, as a function returning its
+    estimated time for the whole workload: the oracle's C map build over every voxel (OpenMP)
+    plus the reference's EXPLICIT_GEMM forward (CPU torch, fp32) over the first ``rows`` rows of
+    the map, its time scaled by M / rows. The sample bounds im2col at 2^27 elements."""
+    sys.path.insert(0, ROOT)
+    from oracle import oracle
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    feats32, weight32 = w.feats.float(), w.weight.float()
+    M, V, Ci = w.num_voxels, w.kernel_volume, int(w.weight.shape[-1])
+    rows = int(min(M, max(4096, (1 << 27) // max(1, V * Ci))))
+
+    def step() -> float:
+        t0 = time.perf_counter()
+        nbr = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation, nthreads=cores)
+        t1 = time.perf_counter()
+        oracle.explicit_gemm_cpu(feats32, nbr[:rows], weight32)
+        t2 = time.perf_counter()
+        return (t1 - t0) + (t2 - t1) * (M / rows)
+
+    sample = (f"{w.name} ({M} voxels): oracle C map build of every voxel (OpenMP, {cores} threads) "
+              f"+ EXPLICIT_GEMM restated on CPU torch fp32 over the first {rows} map rows, conv time "
+              f"scaled x{M / rows:.2f} to the whole workload")
+    return step, cores, sample
+
+
+def _reference_gpu(workload: str, steps: int, warmup: int) -> dict:
+    """The reference's own GPU forward (oracle/ref_gpu.py, a separate process) or why not."""
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    script = os.path.join(ROOT, "oracle", "ref_gpu.py")
+    try:
+        r = subprocess.run([sys.executable, script, "--workload", workload, "--steps", str(steps),
+                            "--warmup", str(warmup)], capture_output=True, text=True, timeout=900)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference GPU run did not finish: {e}"}
+    if r.returncode != 0:
+        tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+        return {"unavailable": f"reference GPU run exited {r.returncode}: {tail[0][:300]}"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            return json.loads(line)
+    return {"unavailable": "reference GPU run printed no result"}
+
+
 def run_reference(args):
     world, rank, _local = _dist()
     if rank != 0:
         return 0
-    sys.path.insert(0, ROOT)
-    from oracle import oracle
     from sparseconv import synthetic
     w = synthetic.make(args.workload, seed=0)
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    feats32 = w.feats.float()
-    weight32 = w.weight.float()
-
-    def step():
-        nbr = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation, nthreads=cores)
-        return oracle.explicit_gemm_cpu(feats32, nbr, weight32)
-
+    ref_gpu = _reference_gpu(args.workload, max(3, min(args.steps, 10)), args.warmup)
+    step, cores, sample = _cpu_sampler(w)
     for _ in range(args.warmup):
         step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
+    times = [step() for _ in range(args.steps)]
     total = float(np.sum(times))
     value = w.num_voxels * args.steps / total
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": dict(w.describe(), l2="n/a (host CPU)"),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"the full {w.name} workload ({w.num_voxels} voxels) per step: "
-                                   "oracle C map build (OpenMP) + EXPLICIT_GEMM restated on CPU torch fp32"},
+        "higher_is_better": True, "scaling": "strong" if args.shard == "batch" else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": _config(w),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_gpu": ref_gpu,
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
 def cpu_baseline(w, budget_s: float = 10.0):
-    sys.path.insert(0, ROOT)
-    from oracle import oracle
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    feats32, weight32 = w.feats.float(), w.weight.float()
+    step, cores, sample = _cpu_sampler(w)
     times = []
     t_start = time.perf_counter()
     while True:
-        t0 = time.perf_counter()
-        nbr = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation, nthreads=cores)
-        oracle.explicit_gemm_cpu(feats32, nbr, weight32)
-        times.append(time.perf_counter() - t0)
+        times.append(step())
         if time.perf_counter() - t_start > budget_s or len(times) >= 20:
             break
     t = float(np.median(times))
     return {"value": w.num_voxels / t, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"full {w.name} workload ({w.num_voxels} voxels), median of {len(times)} runs: "
-                      "oracle C map build (OpenMP) + EXPLICIT_GEMM restated on CPU torch fp32"}
+            "sample": sample + f"; median of {len(times)} runs"}
+
+
+def _batch_local(w, rank: int, world: int):
+    """Rank r's part of the workload's batch: samples b with b % world == r, renumbered
+    b // world, so the rank's grid holds only its own samples."""
+    import dataclasses
+    if world == 1:
+        return w
+    b = w.coords[:, 0]
+    sel = (b % world) == rank
+    coords = np.ascontiguousarray(w.coords[sel])
+    coords[:, 0] //= world
+    B = int(w.shape[0])
+    local_b = len(range(rank, B, world))
+    if local_b == 0:
+        raise ValueError(f"batch {B} has no sample for rank {rank} of {world}")
+    feats = w.feats[torch.from_numpy(np.nonzero(sel)[0])].contiguous()
+    return dataclasses.replace(w, coords=coords, feats=feats, shape=(local_b,) + tuple(w.shape[1:]))
 
 
 def main():
@@ -214,8 +268,11 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="cube")
+    ap.add_argument("--workload", default="indoor")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--shard", default="batch", choices=["batch", "replica"],
+                    help="N>1: split the workload's batch over the ranks (strong scaling) or give "
+                         "every rank its own full batch (weak scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--e2e-streams", type=int, default=2, help="CUDA streams the end-to-end steps rotate over")
@@ -242,7 +299,11 @@ def main():
     from sparseconv import _native, shards, synthetic
     from sparseconv.ops.submanifold_conv3d import Algorithm, sparse_submanifold_conv3d
 
-    w = synthetic.make(args.workload, seed=rank)
+    if args.shard == "batch":
+        w_all = synthetic.make(args.workload, seed=0)
+        w = _batch_local(w_all, rank, world)
+    else:
+        w_all = w = synthetic.make(args.workload, seed=rank)
     coords_h = torch.from_numpy(w.coords).pin_memory()
     feats_h = w.feats.pin_memory()
     coords = coords_h.to(dev)
@@ -456,17 +517,19 @@ def main():
         cached_map = None
         if per_stage.get("conv", (0.0, 0))[0] > 0:
             conv_ms = per_stage["conv"][0] / max(per_stage["conv"][1], 1)
-            cached_map = {"value": w.num_voxels * world / (conv_ms / 1e3), "unit": UNIT,
+            cached_map = {"value": voxels_all / (conv_ms / 1e3), "unit": UNIT,
                           "conv_ms_per_step": conv_ms,
                           "step": "conv kernel alone on a reused map (per-launch CUDA events, L2 flushed)"}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": max_ms / K, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong" if args.shard == "batch" else "weak", "vs_baseline": None,
             "dtype": str(w.dtype).replace("torch.", "").replace("float16", "f16").replace("bfloat16", "bf16").replace("float32", "f32"),
             "data": "synthetic",
-            "config": dict(w.describe(), per_rank=True, l2="flushed between steps (256 MB write)",
-                           nnz_per_voxel=nnz / w.num_voxels, parallelism=f"batch-sharded x{world}"),
+            "config": _config(w_all),
+            "details": {"parallelism": (f"batch split over {world} ranks (samples b % {world} == rank)"
+                                        if args.shard == "batch" else f"{world} replicas, own batch each"),
+                        "rank0_voxels": w.num_voxels, "nnz_per_voxel_rank0": nnz / w.num_voxels},
             "effective": {"tflops_alg": fig["flops_alg"] * world * K / (max_ms / 1e3) / 1e12,
                           "tflops_dense_equivalent": fig["flops_dense"] * world * K / (max_ms / 1e3) / 1e12},
             "stages_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in per_stage.items()},

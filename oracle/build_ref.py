@@ -1,13 +1,21 @@
 """ORACLE -- test infrastructure only.
 
 Compiles the reference's own CUDA kernel-map extension from its sources where they lie
-(``/root/reference/src/sparseconv/kernels/cuda/{hash/hash.cu, neighbor_map/neighbor_map.cu,
-ext.cpp}``) into ``oracle/_ref/sparseconv_ref_cuda.so`` with nvcc/g++ directly (the
-reference's setup.py is not run). The module exposes the reference's four pybind11
-bindings (``ext.cpp:5-10``); GPU tests call its
-``hashmap_build_submanifold_conv_neighbor_map_cuda_naive`` to pin the kernel map of the
+(``src/sparseconv/kernels/cuda/{hash/hash.cu, neighbor_map/neighbor_map.cu, ext.cpp}`` under
+the reference checkout, ``$SPCONV_REFERENCE_ROOT``, default ``/root/reference``) into
+``oracle/_ref/sparseconv_ref_cuda.so`` with nvcc/g++ directly (the reference's setup.py is not
+run). The module exposes the reference's four pybind11 bindings (``ext.cpp:5-10``); GPU tests
+call its ``hashmap_build_submanifold_conv_neighbor_map_cuda_naive`` to pin the kernel map of the
 oracle and of the new library against the reference itself, and
 ``tests/golden/make_ref_maps.py`` uses it to write golden map fixtures.
+
+It also stages the reference's unmodified Python package (``src/sparseconv/**/*.py``: the
+front end, the ops and the Triton implicit-GEMM kernel ``kernels/triton/implicit_gemm.py``)
+under ``oracle/_ref/py/`` next to a two-file stub of ``flex_gemm``, the un-vendored package
+that ``implicit_gemm.py:5-6`` imports but never calls. ``oracle/ref_gpu.py`` runs the
+reference's own GPU forward from there (its public ``sparse_submanifold_conv3d`` with
+``Algorithm.IMPLICIT_GEMM``), so that the reference's B200 time can be measured beside this
+library's. ``oracle/_ref/`` is not committed; it travels with the working tree.
 
 Flags follow the reference's build (``setup.py:22,28-31``: ``-O3 -std=c++17
 --use_fast_math``) with the architecture fixed to sm_100a. The sources are only read.
@@ -26,17 +34,57 @@ OUT_DIR = os.path.join(HERE, "_ref")
 OBJ_DIR = os.path.join(OUT_DIR, "obj")
 MODULE = "sparseconv_ref_cuda"
 OUT = os.path.join(OUT_DIR, MODULE + ".so")
-REF_ROOT = "/root/reference/src/sparseconv/kernels/cuda"
+REF_CHECKOUT = os.environ.get("SPCONV_REFERENCE_ROOT", "/root/reference")
+REF_PKG = os.path.join(REF_CHECKOUT, "src", "sparseconv")
+REF_ROOT = os.path.join(REF_PKG, "kernels", "cuda")
 SOURCES = ["hash/hash.cu", "neighbor_map/neighbor_map.cu", "ext.cpp"]
+PY_DIR = os.path.join(OUT_DIR, "py")          # staged reference Python package + flex_gemm stub
+
+# flex_gemm is imported at module level by implicit_gemm.py:5-6 and never called; the stub
+# makes the import succeed and fails loudly if anything does call it.
+_FLEX_GEMM_STUB = {
+    "flex_gemm/__init__.py": '"""Import stub: the reference imports flex_gemm but never calls it."""\n',
+    "flex_gemm/ops/__init__.py": "",
+    "flex_gemm/ops/spconv.py": (
+        "def sparse_submanifold_conv3d(*args, **kwargs):\n"
+        "    raise NotImplementedError('flex_gemm is not installed; the reference never calls it')\n"),
+}
 
 
 def available() -> bool:
     return os.path.isdir(REF_ROOT)
 
 
+def stage_python(force: bool = False) -> str:
+    """Copy the reference's Python package (``*.py`` only) and the flex_gemm stub into
+    ``oracle/_ref/py``. Returns that directory."""
+    import shutil
+    marker = os.path.join(PY_DIR, "sparseconv", "__init__.py")
+    if os.path.exists(marker) and not force:
+        return PY_DIR
+    if not os.path.isdir(REF_PKG):
+        raise RuntimeError("reference Python package not present; cannot stage oracle/_ref/py")
+    dst_pkg = os.path.join(PY_DIR, "sparseconv")
+    if os.path.isdir(dst_pkg):
+        shutil.rmtree(dst_pkg)
+    for dirpath, _dirs, files in os.walk(REF_PKG):
+        rel = os.path.relpath(dirpath, REF_PKG)
+        for f in files:
+            if f.endswith(".py"):
+                os.makedirs(os.path.join(dst_pkg, rel), exist_ok=True)
+                shutil.copyfile(os.path.join(dirpath, f), os.path.join(dst_pkg, rel, f))
+    for rel, text in _FLEX_GEMM_STUB.items():
+        path = os.path.join(PY_DIR, rel)
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        with open(path, "w") as fh:
+            fh.write(text)
+    return PY_DIR
+
+
 def build(force: bool = False, verbose: bool = True) -> str:
     if not available():
         raise RuntimeError("reference sources not present; cannot build oracle/_ref")
+    stage_python(force)
     if os.path.exists(OUT) and not force:
         return OUT
     import torch
