@@ -167,7 +167,9 @@ int spconv_hashmap_lookup(const void *table_keys, const void *table_values, int6
  *     workspace entry point for them);
  *   - the first call on a device looks up the scratch array's device address for that device
  *     (cudaGetSymbolAddress, with the stream's device current); make that first call before
- *     any stream capture begins;
+ *     any stream capture begins. The address is kept for the life of the process: do not call
+ *     this entry point on a device after cudaDeviceReset (or any other teardown of its primary
+ *     context) in the same process;
  *   - every call on a device shares the one scratch array and leaves it holding that call's
  *     table; each call clears what it uses first. Calls whose execution overlaps on the GPU
  *     (different streams without ordering, or several host threads) race on the array and

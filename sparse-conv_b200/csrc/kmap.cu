@@ -1390,9 +1390,16 @@ namespace spconv {
 
 constexpr int64_t noalloc_capacity() { return capacity_for((int64_t)SPCONV_NOALLOC_MAX_COORDS); }
 constexpr int64_t align256c(int64_t x) { return (x + 255) & ~int64_t(255); }
+// The largest layout ws_layout gives for at most SPCONV_NOALLOC_MAX_COORDS voxels: 64-bit keys
+// (table + row array), no bitmap, histogram and cursors. The radix-sort counts are absent
+// because such inputs stay below kSortMinVoxels (checked below); a 32-bit-key layout is smaller,
+// and its bitmap is dropped when it does not fit.
 constexpr int64_t kNoAllocScratchBytes =
     align256c(noalloc_capacity() * 8) + align256c(noalloc_capacity() * 4) +
     2 * align256c(kOrderBuckets * 4) + 256;
+static_assert((int64_t)SPCONV_NOALLOC_MAX_COORDS < kSortMinVoxels,
+              "the no-alloc scratch has no room for the radix-sort counts: raise "
+              "kNoAllocScratchBytes to cover ws_layout's sort_counts before raising the limit");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -1400,7 +1407,9 @@ constexpr int kNoAllocMaxDevices = 64;
 static std::mutex g_noalloc_mu;
 static void *g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
 
-// Device address of the scratch array on the current device; looked up once per device.
+// Device address of the scratch array on the current device; looked up once per device and
+// kept for the life of the process, so the entry point must not be used on a device after
+// cudaDeviceReset (or anything else that destroys its primary context) in the same process.
 static int noalloc_scratch(void **out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");

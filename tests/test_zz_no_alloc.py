@@ -63,32 +63,58 @@ def _bucket_keys(masks_np):
     return cls * 256 + (h & np.uint64(255)).astype(np.int64)
 
 
+def _check_against_workspace_entry_point(lib, coords_np, shape, ks, dil):
+    coords, nbr, masks, order, status = _noalloc_map(lib, coords_np, shape, ks, dil)
+    N, _C, W, H, D = shape
+    ref_nbr, ref_masks, ref_order = _native.build_neighbor_map(coords, N, W, H, D, ks, dil)
+    torch.cuda.synchronize()
+    assert status == 0
+    assert torch.equal(nbr, ref_nbr)                        # bit-exact map
+    assert torch.equal(masks, ref_masks)                    # bit-exact masks
+    o, ro = order.cpu().numpy(), ref_order.cpu().numpy()
+    assert np.array_equal(np.sort(o), np.arange(len(o), dtype=np.int32))
+    keys = _bucket_keys(masks.cpu().numpy())
+    assert np.array_equal(keys[o], keys[ro])                # same buckets at every position
+    # and the conv gives the same bits over either map / order
+    g = torch.Generator().manual_seed(0)
+    V = nbr.shape[1]
+    feats = torch.randn((nbr.shape[0], 32), generator=g).half().cuda()
+    weight = (torch.randn((32, V, 32), generator=g) * 0.05).half().cuda()
+    a = _native.conv_forward(feats, weight, None, nbr, masks, order)
+    b = _native.conv_forward(feats, weight, None, ref_nbr, ref_masks, ref_order)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
 def test_noalloc_matches_workspace_entry_point_on_two_calls():
     lib = _native.load_library()
     cube = gpu_cases.workload("cube")                       # 168,546 voxels, then a small case
     calls = [(cube.coords, cube.shape, cube.kernel_size, cube.dilation),
              gpu_cases.small_cases()["rand5"]]
     for coords_np, shape, ks, dil in calls:
-        coords, nbr, masks, order, status = _noalloc_map(lib, coords_np, shape, ks, dil)
-        N, _C, W, H, D = shape
-        ref_nbr, ref_masks, ref_order = _native.build_neighbor_map(coords, N, W, H, D, ks, dil)
-        torch.cuda.synchronize()
-        assert status == 0
-        assert torch.equal(nbr, ref_nbr)                    # bit-exact map
-        assert torch.equal(masks, ref_masks)                # bit-exact masks
-        o, ro = order.cpu().numpy(), ref_order.cpu().numpy()
-        assert np.array_equal(np.sort(o), np.arange(len(o), dtype=np.int32))
-        keys = _bucket_keys(masks.cpu().numpy())
-        assert np.array_equal(keys[o], keys[ro])            # same buckets at every position
-        # and the conv gives the same bits over either map / order
-        g = torch.Generator().manual_seed(0)
-        V = nbr.shape[1]
-        feats = torch.randn((nbr.shape[0], 32), generator=g).half().cuda()
-        weight = (torch.randn((32, V, 32), generator=g) * 0.05).half().cuda()
-        a = _native.conv_forward(feats, weight, None, nbr, masks, order)
-        b = _native.conv_forward(feats, weight, None, ref_nbr, ref_masks, ref_order)
-        torch.cuda.synchronize()
-        assert torch.equal(a, b)
+        _check_against_workspace_entry_point(lib, coords_np, shape, ks, dil)
+
+
+def _limit_sized_coords(seed=11):
+    """Exactly SPCONV_NOALLOC_MAX_COORDS distinct voxels of a 2 x 128^3 grid, sorted."""
+    rng = np.random.default_rng(seed)
+    cells = np.sort(rng.choice(2 * 128 ** 3, size=_native.NOALLOC_MAX_COORDS, replace=False))
+    b, r = np.divmod(cells, 128 ** 3)
+    x, r = np.divmod(r, 128 ** 2)
+    y, z = np.divmod(r, 128)
+    return np.ascontiguousarray(np.stack([b, x, y, z], 1).astype(np.int32)), (2, 1, 128, 128, 128)
+
+
+def test_noalloc_64bit_keys_then_limit_sized_input():
+    """The 64-bit-key layout (grid volume >= 2^32), the one that sets the scratch size, and then
+    an input of exactly the entry point's limit, again two calls in a row."""
+    lib = _native.load_library()
+    c64, s64 = gpu_cases.key64_coords(8)
+    assert s64[0] * s64[2] * s64[3] * s64[4] >= 2 ** 32
+    climit, slimit = _limit_sized_coords()
+    assert climit.shape[0] == _native.NOALLOC_MAX_COORDS
+    for coords_np, shape in ((c64, s64), (climit, slimit)):
+        _check_against_workspace_entry_point(lib, coords_np, shape, (3, 3, 3), (1, 1, 1))
 
 
 def test_noalloc_rejects_inputs_over_its_limit():
