@@ -58,6 +58,14 @@ extern "C" {
 
 int spconv_abi_version(void);
 
+/* Time limit, in nanoseconds, of the pipeline waits inside the tensor-core conv kernels
+ * launched after this call (process-wide; default 2 s; 0 restores the default). A wait that
+ * reaches it makes the kernel abandon its work, wait (bounded) for its own copies and MMAs,
+ * free its tensor memory, return, and set SPCONV_STATUS_WAIT_TIMEOUT; the context stays
+ * usable. Returns the previous limit. Lowering it is for tests of that path.
+ * No counterpart in the reference (its probe loops have no bound). */
+uint64_t spconv_set_wait_limit_ns(uint64_t limit_ns);
+
 /* Message of the last host-side error on the calling thread ("" if none). */
 const char *spconv_last_error(void);
 

@@ -1,5 +1,6 @@
 // C-ABI plumbing shared by every entry point: version, per-thread error message, and
 // the launch check that turns a failed CUDA launch into SPCONV_ERR_CUDA.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -10,6 +11,9 @@
 namespace spconv {
 
 static thread_local char g_last_error[512] = "";
+static std::atomic<uint64_t> g_wait_limit_ns{kWaitLimitNs};
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 void set_error(const char *fmt, ...) {
     va_list ap;
@@ -99,5 +103,10 @@ extern "C" int spconv_stage_times_ms(double *total_ms, int64_t *launches, int n)
 }
 
 extern "C" int spconv_abi_version(void) { return SPCONV_ABI_VERSION; }
+
+extern "C" uint64_t spconv_set_wait_limit_ns(uint64_t limit_ns) {
+    const uint64_t v = limit_ns == 0 ? spconv::kWaitLimitNs : limit_ns;
+    return spconv::g_wait_limit_ns.exchange(v);
+}
 
 extern "C" const char *spconv_last_error(void) { return spconv::g_last_error; }

@@ -41,9 +41,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
-// Upper bound on any spin-wait inside a kernel. A wait that exceeds it raises
-// SPCONV_STATUS_WAIT_TIMEOUT and the kernel abandons its remaining work.
+// Default upper bound on a spin-wait inside a kernel. A wait that exceeds its limit raises
+// SPCONV_STATUS_WAIT_TIMEOUT and the kernel abandons its remaining work. The limit of the
+// pipeline waits is a kernel argument (spconv_set_wait_limit_ns sets it for later launches);
+// the clean-up waits of an abandoned kernel (for its own copies and MMAs, which always
+// complete) keep this fixed bound.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
+// The pipeline-wait limit the next conv launches pass to their kernels (process-wide).
+uint64_t wait_limit_ns();
 
 // 32-bit murmur3 finaliser (a well-mixed bijection on uint32).
 __device__ __forceinline__ uint32_t fmix32(uint32_t k) {
@@ -197,13 +202,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 // Bounded wait that also gives up when another role of the CTA has flagged an abort.
 // On timeout it sets the flag itself. Returns false when the caller must abandon its work.
 __device__ __forceinline__ bool mbar_wait_or_abort(uint32_t addr, uint32_t parity,
-                                                   volatile int *abort_flag) {
+                                                   volatile int *abort_flag, uint64_t limit_ns) {
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         if (mbar_try_wait(addr, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             *abort_flag = 1;
             return false;
         }

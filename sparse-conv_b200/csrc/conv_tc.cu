@@ -6,28 +6,30 @@
 // A tile is 128 consecutive entries of the voxel order produced by the map build, so its rows
 // share most of their offset masks; the OR of the 128 masks selects the offsets the tile needs.
 // The work of a CTA is a stream of steps, one per (tile, active offset v, K chunk of <= 64
-// channels). One CTA = 10 warps with fixed roles, synchronised only through mbarriers:
+// channels). One CTA = NG + 6 warps (NG = 4 or 8 gatherers) with fixed roles, synchronised
+// only through mbarriers:
 //   warp 0    scheduler: per tile, loads its rows (order) and mask words, ORs them, and splits
 //             the active offsets into contexts of <= 16; for each context it loads the 16 x 128
 //             neighbour indices (only where a row's mask bit is set; -1 elsewhere) into one of
 //             three context buffers by cp.async and hands the buffer over;
-//   warps 1-4 gatherers: warp g owns tile rows 32g..32g+31 and runs its own cp.async pipeline:
+//   warps 1..NG gatherers: warp g owns tile rows (128/NG)g .. and runs its own cp.async pipeline:
 //             per step, groups of KC/8 lanes copy whole feature rows (16 B per lane, zero-fill
 //             for a missing neighbour) into the A stage, straight into the 32/64/128-byte
 //             swizzled K-major layout; a step is signalled on the stage's "full" mbarrier once
 //             its copies have landed (cp.async.wait_group, proxy fence, arrive), D-1 steps
 //             behind the issue, so several steps per warp are in flight; warp 1 lane 0 also
-//             loads W[:, v, kc] into the B stage by TMA (bytes counted on the same mbarrier);
-//   warp 5    MMA: one thread waits for a full stage, issues KC/16 tcgen05.mma
-//             (M=128, N=Co, K=16) into the tile's TMEM accumulator, and commits to the stage's
-//             "empty" mbarrier (and, after a tile's last step, to the accumulator's);
-//   warps 6-9 epilogue: TMEM lanes 32*(w%4).. -> registers, + bias, one rounding, one 16-byte
-//             store per 8 outputs; two accumulators alternate so the next tile's MMAs run while
-//             a tile is written out.
+//             loads W[:, v, kc] into the B stage by TMA, counted on the stage's "wfull" mbarrier;
+//   warp NG+1 MMA: one thread waits for a full stage (rows and weights), issues KC/16
+//             tcgen05.mma (M=128, N=Co, K=16) into the tile's TMEM accumulator, and commits to
+//             the stage's "empty" mbarrier (and, after a tile's last step, to the accumulator's);
+//   warps NG+2..NG+5 epilogue: TMEM lanes 32*(w%4).. -> registers, + bias, one rounding, one
+//             16-byte store per 8 outputs; two accumulators alternate so the next tile's MMAs
+//             run while a tile is written out.
 // Gatherers never wait on the scheduler while holding landed-but-unsignalled steps (they
-// flush first), so no wait depends on itself. Every wait is bounded (2 s); a timeout sets an
-// abort flag that ends every role, raises SPCONV_STATUS_WAIT_TIMEOUT, and the CTA waits
-// (bounded) for its copies and MMAs before it frees TMEM and exits.
+// flush first), so no wait depends on itself. Every wait is bounded (2 s by default, a kernel
+// argument); a timeout sets an abort flag that ends every role, raises
+// SPCONV_STATUS_WAIT_TIMEOUT, and the CTA waits (bounded) for its copies, weight loads, MMAs
+// and accumulator commits before it frees TMEM and exits.
 #include <cuda.h>
 #include <mutex>
 
@@ -36,8 +38,6 @@
 
 namespace spconv {
 
-constexpr int kTcWarps = 10;
-constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTileM = 128;
 constexpr int kChunk = 16;          // active offsets per context
 constexpr int kNPitch = kChunk + 1; // words per row in a context buffer (conflict-free both ways)
@@ -48,8 +48,15 @@ constexpr int kCtxBufs = 3;
 constexpr int kTileRing = 4;        // tiles whose rows the epilogue may still need
 constexpr int kMaxMaskWords = 4;    // offset masks are used for V <= 128 (else all offsets run)
 constexpr int kMaxStages = 8;
-constexpr int kGatherWarps = 4;
-constexpr int kWarpSched = 0, kWarpGather = 1, kWarpMma = 5, kWarpEpi = 6;
+// mbarriers: full[8] empty[8] cfull[3] cempty[3] afull[2] aempty[2] tfull[4] tempty[4] wfull[8]
+constexpr int kNumBars = 42;
+// Warp roles for NG gatherer warps: scheduler 0, gatherers 1..NG, MMA NG+1, epilogue NG+2..NG+5.
+constexpr int kWarpSched = 0, kWarpGather = 1;
+template <int NG> struct TcRoles {
+    static constexpr int kWarpMma = NG + 1, kWarpEpi = NG + 2;
+    static constexpr int kWarps = NG + 6, kThreads = kWarps * 32;
+    static constexpr int kRowsPerWarp = kTileM / NG;
+};
 constexpr uint32_t kInfoFirst = 1u << 30, kInfoLast = 1u << 31, kInfoEnd = 0x3fffffffu;
 constexpr int kCtxFirst = 1, kCtxLast = 2, kCtxRows = 4, kCtxEnd = 8;
 // Tiles with more active offsets than this stage whole index rows (when V <= kRowsMaxV): one
@@ -73,7 +80,7 @@ struct TcCfg {
     static_assert(kRowWindow >= kNPitch, "context buffer");
     static constexpr int kSchedBytes = kTileM + kCtxBufs * kTileM;           // active list, row shifts
     static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kActMax * 4 + kCtxBufs * 16 +
-                                       kTileRing * kTileM * 4 + kMaxStages * 4 + 40 * 8 + 16;
+                                       kTileRing * kTileM * 4 + kMaxStages * 4 + kNumBars * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
     static constexpr int kBudget = kStageBytes <= 12 * 1024 ? 110 * 1024 : 219 * 1024;
     static constexpr int kMinBlocks = kStageBytes <= 12 * 1024 ? 2 : 1;   // registers for two CTAs
@@ -91,7 +98,7 @@ struct TcCfg {
     static constexpr int kOffTRow = kOffCInfo + kCtxBufs * 16;
     static constexpr int kOffInfo = kOffTRow + kTileRing * kTileM * 4;
     static constexpr int kOffBar = kOffInfo + kMaxStages * 4;
-    static constexpr int kOffMisc = kOffBar + 40 * 8;
+    static constexpr int kOffMisc = kOffBar + kNumBars * 8;
     static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
     static constexpr int kTmemCols = 2 * CO < 32 ? 32 : 2 * CO;   // two accumulators
     static constexpr int kMaxCtasByTmem = 512 / kTmemCols;
@@ -126,16 +133,21 @@ __device__ __forceinline__ uint32_t sel4(uint32_t a, uint32_t b, uint32_t c, uin
     return w == 0 ? a : (w == 1 ? b : (w == 2 ? c : d));
 }
 
-template <int CI, int CO, typename T, bool FLIP>
-__global__ void __launch_bounds__(kTcThreads, TcCfg<CI, CO>::kMinBlocks)
+template <int CI, int CO, typename T, bool FLIP, int NG>
+__global__ void __launch_bounds__(TcRoles<NG>::kThreads, TcCfg<CI, CO>::kMinBlocks)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__ feats,
                const T *__restrict__ bias, const int32_t *__restrict__ nbr,
                const uint32_t *__restrict__ masks, const int32_t *__restrict__ order,
                T *__restrict__ out, int64_t M, int V, int MW, int MWS, int num_tiles, int row_mode,
-               int32_t *status) {
+               int32_t *status, uint64_t wait_ns) {
     using Cfg = TcCfg<CI, CO>;
+    using Roles = TcRoles<NG>;
     constexpr int S = Cfg::kStages, KC = Cfg::KC, NKC = Cfg::NKC, RB = Cfg::kRowBytes;
     constexpr int LPR = Cfg::kLanesPerRow, D = Cfg::kDepth;
+    constexpr int kWarpMma = Roles::kWarpMma, kWarpEpi = Roles::kWarpEpi, RPW = Roles::kRowsPerWarp;
+    // rows per lane: each warp instruction moves 32 / LPR whole rows, NQ instructions per step
+    constexpr int NQ = RPW * LPR / 32;
+    static_assert(NQ >= 1 && NQ * 32 == RPW * LPR && (NQ & (NQ - 1)) == 0, "gatherer row split");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const uint32_t sA = smem_u32(base + Cfg::kOffA), sB = smem_u32(base + Cfg::kOffB);
@@ -149,18 +161,20 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     uint64_t *bar = reinterpret_cast<uint64_t *>(base + Cfg::kOffBar);
     uint64_t *full = bar, *empty = bar + 8, *cfull = bar + 16, *cempty = bar + 19;
     uint64_t *afull = bar + 22, *aempty = bar + 24, *tfull = bar + 26, *tempty = bar + 30;
+    uint64_t *wfull = bar + 34;    // per stage: the weight tile's TMA bytes (and the step info)
     uint32_t *s_tmem = reinterpret_cast<uint32_t *>(base + Cfg::kOffMisc);
     volatile int *s_abort = reinterpret_cast<volatile int *>(base + Cfg::kOffMisc + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(&full[s]), kGatherWarps + 1);
+            mbar_init(smem_u32(&full[s]), NG);
             mbar_init(smem_u32(&empty[s]), 1);
+            mbar_init(smem_u32(&wfull[s]), 1);
         }
         for (int c = 0; c < kCtxBufs; ++c) {
             mbar_init(smem_u32(&cfull[c]), 1);
-            mbar_init(smem_u32(&cempty[c]), kGatherWarps);
+            mbar_init(smem_u32(&cempty[c]), NG);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&afull[b]), 1);
@@ -193,7 +207,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     auto tile_id = [&](int k) { return k == 0 ? G - 1 - (int)blockIdx.x : (int)blockIdx.x + k * G; };
     const bool use_masks = MWS > 0;
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
-        return mbar_wait_or_abort(smem_u32(b), parity, s_abort);
+        return mbar_wait_or_abort(smem_u32(b), parity, s_abort, wait_ns);
     };
 
     if (warp == kWarpSched) {
@@ -387,18 +401,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             }
         }
         cp_async_wait_all();
-    } else if (warp >= kWarpGather && warp < kWarpGather + kGatherWarps) {
+    } else if (warp >= kWarpGather && warp < kWarpGather + NG) {
         // ------------------------------------------------------------------ gatherers
-        // Lane L copies chunk L % LPR of tile rows 32g + (L / LPR) * LPR + q, q < LPR: each
-        // warp instruction moves 32 / LPR whole rows, and a lane's LPR neighbour indices are
-        // consecutive in the context buffer.
+        // Warp g owns tile rows RPW*g .. RPW*g + RPW - 1. Lane L copies chunk L % LPR of rows
+        // RPW*g + (L / LPR) * NQ + q, q < NQ: each warp instruction moves 32 / LPR whole rows,
+        // and a lane's NQ neighbour indices are consecutive in the context buffer.
         const int gw = warp - kWarpGather;
         const bool b_loader = gw == 0 && lane == 0;
         const int chunk = lane % LPR;
-        const int row0 = 32 * gw + (lane / LPR) * LPR;       // first of this lane's rows
-        uint32_t dst[LPR];
+        const int row0 = RPW * gw + (lane / LPR) * NQ;       // first of this lane's rows
+        uint32_t dst[NQ];
 #pragma unroll
-        for (int q = 0; q < LPR; ++q) {
+        for (int q = 0; q < NQ; ++q) {
             const int r = row0 + q;
             dst[q] = (uint32_t)(r * RB + ((chunk ^ ((r * RB >> 7) & (LPR - 1))) << 4));
         }
@@ -424,30 +438,32 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             const int k = ci.x, cnt = ci.y;
             const bool cfirst = (ci.z & kCtxFirst) != 0, clast = (ci.z & kCtxLast) != 0;
             const bool crows = (ci.z & kCtxRows) != 0;
-            // row mode: the rotations of this lane's LPR rows, one byte each
-            uint32_t rotw[(LPR + 3) / 4];
+            // row mode: the rotations of this lane's NQ rows, one byte each
+            uint32_t rotw[(NQ + 3) / 4];
             if (Cfg::kRows && crows) {
-                if constexpr (LPR >= 4) {
+                if constexpr (NQ >= 4) {
 #pragma unroll
-                    for (int w = 0; w < LPR / 4; ++w)
+                    for (int w = 0; w < NQ / 4; ++w)
                         rotw[w] = reinterpret_cast<const uint32_t *>(s_mis + cb * kTileM + row0)[w];
-                } else {
+                } else if constexpr (NQ == 2) {
                     rotw[0] = *reinterpret_cast<const uint16_t *>(s_mis + cb * kTileM + row0);
+                } else {
+                    rotw[0] = s_mis[cb * kTileM + row0];
                 }
             }
             const int32_t *rowp = &s_n[(cb * kTileM + row0) * kRowWindow];
             for (int i = 0; i < cnt && ok; ++i) {
                 const int v = s_act[cb * kActMax + i];
-                int32_t n[LPR];
+                int32_t n[NQ];
                 if (Cfg::kRows && crows) {
                     const int vc = FLIP ? V - 1 - v : v;      // the map column of offset v
 #pragma unroll
-                    for (int q = 0; q < LPR; ++q)
+                    for (int q = 0; q < NQ; ++q)
                         n[q] = rowp[q * kRowWindow + ((vc + (int)(rotw[q >> 2] >> (8 * (q & 3)))) & 31)];
                 } else {
                     const int32_t *np = &s_n[cb * Cfg::kBufWords + row0 * kNPitch + i];
 #pragma unroll
-                    for (int q = 0; q < LPR; ++q) n[q] = np[q * kNPitch];
+                    for (int q = 0; q < NQ; ++q) n[q] = np[q * kNPitch];
                 }
 #pragma unroll
                 for (int kc = 0; kc < NKC; ++kc) {
@@ -456,13 +472,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                     if (b_loader) {
                         s_info[s] = (uint32_t)k | ((cfirst && i == 0 && kc == 0) ? kInfoFirst : 0u) |
                                     ((clast && i == cnt - 1 && kc == NKC - 1) ? kInfoLast : 0u);
-                        mbar_arrive_expect_tx(smem_u32(&full[s]), (uint32_t)Cfg::kBBytes);
-                        tma_load_2d(sB + s * Cfg::kBBytes, &tmap_w, v * CI + kc * KC, 0, smem_u32(&full[s]));
+                        mbar_arrive_expect_tx(smem_u32(&wfull[s]), (uint32_t)Cfg::kBBytes);
+                        tma_load_2d(sB + s * Cfg::kBBytes, &tmap_w, v * CI + kc * KC, 0, smem_u32(&wfull[s]));
                     }
                     const uint32_t a_st = sA + s * Cfg::kABytes;
                     const T *src = feats + kc * KC + chunk * 8;
 #pragma unroll
-                    for (int q = 0; q < LPR; ++q) {
+                    for (int q = 0; q < NQ; ++q) {
                         // rows outside the feature table (and missing neighbours) read as zeros
                         const bool have = (uint32_t)n[q] < (uint32_t)M;
                         cp_async_16(a_st + dst[q], src + (int64_t)(have ? n[q] : 0) * CI, have ? 16u : 0u);
@@ -487,7 +503,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             if (u == 0 || wait(&empty[s], (uint32_t)((u - 1) & 1))) {
                 if (b_loader) {
                     s_info[s] = kInfoEnd;
-                    mbar_arrive(smem_u32(&full[s]));
+                    mbar_arrive(smem_u32(&wfull[s]));
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&full[s]));
@@ -495,10 +511,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
         }
         cp_async_wait_all();
         if (!ok && b_loader) {
-            // wait (bounded) for the weight loads of the last step issued on each stage
+            // wait (bounded) for the weight loads of the last step issued on each stage; each
+            // has a barrier of its own, so these waits end as soon as the bytes have landed
             for (int q = 1; q <= S && q <= step; ++q) {
                 const int st = step - q;
-                mbar_wait_bounded(smem_u32(&full[st % S]), (uint32_t)((st / S) & 1));
+                mbar_wait_bounded(smem_u32(&wfull[st % S]), (uint32_t)((st / S) & 1));
             }
         }
     } else if (warp == kWarpMma) {
@@ -506,9 +523,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
         if (lane == 0) {
             const uint32_t idesc = instr_desc_f16(dtype_traits<T>::mma_format, kTileM, CO);
             int step = 0;
+            int acc0 = 0, acc1 = 0;          // commits made to afull[0], afull[1]
             for (;;) {
                 const int s = step % S, u = step / S;
-                if (!wait(&full[s], (uint32_t)(u & 1))) break;
+                if (!wait(&full[s], (uint32_t)(u & 1))) break;       // the A rows
+                if (!wait(&wfull[s], (uint32_t)(u & 1))) break;      // the weight tile, the step info
                 const uint32_t info = s_info[s];
                 if (info == kInfoEnd) break;
                 const int k = (int)(info & 0x3fffffffu);
@@ -524,12 +543,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                     tc_mma_f16(d, ad, bd, idesc, (!first || kk > 0) ? 1u : 0u);
                 }
                 tc_commit(smem_u32(&empty[s]));
-                if (last) tc_commit(smem_u32(&afull[b]));
+                if (last) {
+                    tc_commit(smem_u32(&afull[b]));
+                    if (b) ++acc1; else ++acc0;
+                }
                 ++step;
             }
             if (*s_abort && step > 0) {      // wait (bounded) for the MMAs issued so far
                 const int st = step - 1;
                 mbar_wait_bounded(smem_u32(&empty[st % S]), (uint32_t)((st / S) & 1));
+                // and for the accumulator commits, whose arrivals must not outlive the CTA
+                if (acc0 > 0) mbar_wait_bounded(smem_u32(&afull[0]), (uint32_t)((acc0 - 1) & 1));
+                if (acc1 > 0) mbar_wait_bounded(smem_u32(&afull[1]), (uint32_t)((acc1 - 1) & 1));
             }
         }
     } else if (warp >= kWarpEpi) {
@@ -631,10 +656,22 @@ static bool make_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t cols, uint6
     return true;
 }
 
+// Gatherer warps: eight where a CTA has an SM to itself (large stages), four where two CTAs
+// share one. Two gatherer warps per SM sub-partition keep more cp.async issue in flight than
+// one: a gatherer's step is a short dependent chain (index, address, copy, commit, wait).
+#ifndef SPCONV_TC_GATHER_WARPS_1CTA
+#define SPCONV_TC_GATHER_WARPS_1CTA 8
+#endif
+#ifndef SPCONV_TC_GATHER_WARPS_2CTA
+#define SPCONV_TC_GATHER_WARPS_2CTA 4
+#endif
+
 template <int CI, int CO, typename T, bool FLIP>
 static int launch_tc_k(const ConvArgs &a) {
     using Cfg = TcCfg<CI, CO>;
-    auto kern = conv_tc_kernel<CI, CO, T, FLIP>;
+    constexpr int NG = Cfg::kMinBlocks >= 2 ? SPCONV_TC_GATHER_WARPS_2CTA : SPCONV_TC_GATHER_WARPS_1CTA;
+    constexpr int kThreads = TcRoles<NG>::kThreads;
+    auto kern = conv_tc_kernel<CI, CO, T, FLIP, NG>;
     const int MWS = (a.masks && a.MW <= kMaxMaskWords) ? a.MW : 0;
     // Shared memory is padded so that no more CTAs fit on an SM than its 512 TMEM columns
     // serve (228 KB of shared memory per SM, 1 KB reserved per CTA): tcgen05.alloc never waits.
@@ -655,7 +692,7 @@ static int launch_tc_k(const ConvArgs &a) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return check_launch("conv_tc: set shared memory carveout");
-        int occ = occupancy_per_sm((const void *)kern, kTcThreads, smem);
+        int occ = occupancy_per_sm((const void *)kern, kThreads, smem);
         if (occ > Cfg::kMaxCtasByTmem) occ = Cfg::kMaxCtasByTmem;
         occ_cache[dev] = occ < 1 ? 1 : occ;
         attr_done[dev] = true;
@@ -673,9 +710,9 @@ static int launch_tc_k(const ConvArgs &a) {
     if (grid < 1) grid = 1;
     // Whole index rows are staged when one fits a 128-byte window and the map is 16-byte aligned.
     const int row_mode = (a.V <= kRowsMaxV && ((uintptr_t)a.nbr & 15u) == 0) ? 1 : 0;
-    const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kTcThreads), (size_t)smem, a.stream, tw,
+    const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kThreads), (size_t)smem, a.stream, tw,
                                       (const T *)a.feats, (const T *)a.bias, a.nbr, a.masks, a.order, (T *)a.out,
-                                      a.M, a.V, a.MW, MWS, num_tiles, row_mode, a.status);
+                                      a.M, a.V, a.MW, MWS, num_tiles, row_mode, a.status, wait_limit_ns());
     if (le != cudaSuccess) return check_launch("conv_tc_kernel launch");
     return check_launch("conv_tc_kernel");
 }

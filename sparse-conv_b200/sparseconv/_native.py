@@ -75,6 +75,7 @@ SIGNATURES = {
     "spconv_submanifold_conv_weight_grad": (_c_int, [
         _c_void_p, _c_void_p, _c_int, _c_i64, _c_int, _c_int, _c_int,
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_i64, _c_void_p, _c_void_p]),
+    "spconv_set_wait_limit_ns": (ctypes.c_uint64, [ctypes.c_uint64]),
     "spconv_stage_timing": (_c_int, [_c_int]),
     "spconv_stage_times_ms": (_c_int, [_c_void_p, _c_void_p, _c_int]),
 }
@@ -581,6 +582,13 @@ def conv_weight_grad(feats: torch.Tensor, grad_out: torch.Tensor, nbr: torch.Ten
     if rc != SPCONV_OK:
         _raise(rc, "spconv_submanifold_conv_weight_grad")
     return gw, gb
+
+
+def set_wait_limit_ns(limit_ns: int) -> int:
+    """Time limit of the pipeline waits inside the tensor-core conv kernels launched from now
+    on (process-wide; 0 restores the 2 s default). Returns the previous limit. A kernel whose
+    wait reaches it abandons its work and reports SPCONV_STATUS_WAIT_TIMEOUT."""
+    return int(load_library().spconv_set_wait_limit_ns(int(limit_ns)))
 
 
 def stage_timing(max_calls: int) -> None:

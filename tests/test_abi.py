@@ -101,3 +101,11 @@ def test_argument_validation_before_any_launch(lib):
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _native.load_library(str(tmp_path / "absent.so"))
+
+
+def test_wait_limit_setter_round_trip(lib):
+    default = _native.set_wait_limit_ns(0)            # 0 restores the default
+    assert default == 2_000_000_000
+    assert _native.set_wait_limit_ns(12345) == default
+    assert _native.set_wait_limit_ns(0) == 12345
+    assert _native.set_wait_limit_ns(0) == default
