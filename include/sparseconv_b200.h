@@ -214,6 +214,26 @@ int spconv_submanifold_conv_forward_ex(
     const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
     void *out, int32_t *status, void *stream, int kernel_choice);
 
+/* Split-K forward: the same result as spconv_submanifold_conv_forward (within fp32 rounding),
+ * with the heaviest tiles' work spread over two CTAs. Of the first 256 tiles of 128 voxels
+ * that the tensor-core kernel takes (the end of the voxel order, where the voxels with the most
+ * neighbours sort), each one with more than 16 active offsets runs as two halves of its
+ * offsets on different CTAs; each half writes fp32 partial rows into `workspace`, and the
+ * second half to finish adds the two (fp32 addition of two terms commutes, so results do not
+ * vary from run to run) and writes the output. Rows of split tiles therefore round
+ * differently from the unsplit kernel's, within the same tolerance. For shapes or dtypes
+ * the tensor-core kernel does not cover it runs the ordinary kernel (nothing to split).
+ *   workspace: 256-byte aligned, spconv_conv_splitk_workspace_bytes(num_coords, Co) bytes.
+ * Replaces the reference's empty IMPLICIT_GEMM_SPLITK / MASKED_IMPLICIT_GEMM_SPLITK slots
+ * (ops/submanifold_conv3d.py:13-15, 94-99). */
+int64_t spconv_conv_splitk_workspace_bytes(int64_t num_coords, int Co);
+int spconv_submanifold_conv_forward_splitk(
+    const void *feats, int dtype, int64_t num_coords, int Ci,
+    const void *weight, const void *bias, int Co, int kernel_volume,
+    const int32_t *neighbor_map, const uint32_t *masks, const int32_t *order,
+    void *workspace, int64_t workspace_bytes,
+    void *out, int32_t *status, void *stream);
+
 /* Input gradient of the submanifold conv:
  *   grad_in[j, ci] = sum_v sum_co grad_out[nbr_t[j, v], co] * weight_t[ci, v, co]
  * with weight_t[ci, v, co] = weight[co, v, ci] and nbr_t the transposed map. For odd kernel

@@ -134,6 +134,44 @@ static int launch_conv(const ConvArgs &a, int kernel_choice) {
     return launch_conv_simt(a);
 }
 
+extern "C" int64_t spconv_conv_splitk_workspace_bytes(int64_t num_coords, int Co) {
+    if (num_coords < 0 || Co <= 0) return -1;
+    return conv_split_workspace_bytes(num_coords, Co);
+}
+
+extern "C" int spconv_submanifold_conv_forward_splitk(
+    const void *feats, int dtype, int64_t M, int Ci,
+    const void *weight, const void *bias, int Co, int V,
+    const int32_t *nbr, const uint32_t *masks, const int32_t *order,
+    void *workspace, int64_t workspace_bytes,
+    void *out, int32_t *status, void *stream) {
+    SPCONV_REQUIRE(M >= 0 && M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld out of range", (long long)M);
+    SPCONV_REQUIRE(Ci > 0 && Co > 0, SPCONV_ERR_ARG, "channels must be positive (Ci=%d Co=%d)", Ci, Co);
+    SPCONV_REQUIRE(V > 0 && V <= 1024, SPCONV_ERR_ARG, "kernel volume %d out of range [1, 1024]", V);
+    SPCONV_REQUIRE(dtype == SPCONV_F32 || dtype == SPCONV_F16 || dtype == SPCONV_BF16,
+                   SPCONV_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (M == 0) return SPCONV_OK;
+    SPCONV_REQUIRE(feats && weight && nbr && out, SPCONV_ERR_ARG, "null pointer argument");
+    ConvArgs a{feats, dtype, M, Ci, weight, bias, Co, V, spconv_mask_words(V), nbr, masks, order,
+               out, status, (cudaStream_t)stream};
+    const bool tc = tc_supported(dtype, Ci, Co, V) && ((uintptr_t)feats & 15u) == 0 &&
+                    ((uintptr_t)weight & 15u) == 0 && ((uintptr_t)out & 15u) == 0;
+    stage_mark(SPCONV_STAGE_CONV, 0, a.stream);
+    int rc;
+    if (tc) {
+        const int64_t need = conv_split_workspace_bytes(M, Co);
+        SPCONV_REQUIRE(workspace && ((uintptr_t)workspace & 255u) == 0 && workspace_bytes >= need, SPCONV_ERR_ARG,
+                       "split-K workspace must be 256-byte aligned and hold %lld bytes (got %lld)",
+                       (long long)need, (long long)workspace_bytes);
+        a.split_ws = workspace;
+        rc = launch_conv_tc(a);
+    } else {
+        rc = launch_conv(a, SPCONV_KERNEL_AUTO);   // no tensor-core kernel: nothing to split
+    }
+    if (rc == SPCONV_OK) stage_mark(SPCONV_STAGE_CONV, 1, a.stream);
+    return rc;
+}
+
 extern "C" int spconv_submanifold_conv_backward_input(
     const void *grad_out, int dtype, int64_t M, int Co, const void *weight_t, int Ci, int V,
     const int32_t *nbr, const uint32_t *masks, const int32_t *order,

@@ -25,6 +25,9 @@ struct ConvArgs {
     // 1: read the map with offsets reversed (column V-1-v for offset v) and the masks likewise:
     // for odd kernel sizes that is the transposed map, so the input gradient needs no copy
     int flip = 0;
+    // non-null: tcgen05 kernel with split tiles, this workspace holding the per-tile counters
+    // and fp32 partials (conv_split_workspace_bytes)
+    void *split_ws = nullptr;
 };
 
 bool tc_supported(int dtype, int Ci, int Co, int V);
@@ -34,6 +37,8 @@ bool tc_supported(int dtype, int Ci, int Co, int V);
 // per-CTA reservation, registers at warp granularity, threads, CTAs).
 int occupancy_per_sm(const void *kern, int threads, int smem_dynamic);
 int launch_conv_tc(const ConvArgs &a);
+int64_t split_counter_bytes();
+int64_t conv_split_workspace_bytes(int64_t M, int Co);
 int launch_conv_simt(const ConvArgs &a);
 
 }  // namespace spconv

@@ -62,6 +62,12 @@ constexpr int kCtxFirst = 1, kCtxLast = 2, kCtxRows = 4, kCtxEnd = 8;
 // Tiles with more active offsets than this stage whole index rows (when V <= kRowsMaxV): one
 // 128-byte window per voxel costs about what a context of 5..8 offsets does.
 constexpr int kRowsMinAct = 9;
+// Split tiles (SPLIT kernels): of the first kSplitMaxTiles tiles taken (the heaviest: the voxel
+// order sorts voxels by neighbour count), those with more than kSplitMinAct active offsets run
+// as two work items, each over one half of the tile's offsets, on different CTAs.
+constexpr int kSplitMinAct = 16;
+constexpr int kSplitMaxTiles = 256;
+constexpr int kTileEnd = -2;        // tile-ring info of the epilogue's end marker
 
 template <int CI, int CO>
 struct TcCfg {
@@ -80,7 +86,7 @@ struct TcCfg {
     static_assert(kRowWindow >= kNPitch, "context buffer");
     static constexpr int kSchedBytes = kTileM + kCtxBufs * kTileM;           // active list, row shifts
     static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kActMax * 4 + kCtxBufs * 16 +
-                                       kTileRing * kTileM * 4 + kMaxStages * 4 + kNumBars * 8 + 16;
+                                       kTileRing * kTileM * 4 + kTileRing * 4 + kMaxStages * 4 + kNumBars * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
     static constexpr int kBudget = kStageBytes <= 12 * 1024 ? 110 * 1024 : 219 * 1024;
     static constexpr int kMinBlocks = kStageBytes <= 12 * 1024 ? 2 : 1;   // registers for two CTAs
@@ -96,7 +102,8 @@ struct TcCfg {
     static constexpr int kOffAct = kOffMis + kCtxBufs * kTileM;
     static constexpr int kOffCInfo = kOffAct + kCtxBufs * kActMax * 4;
     static constexpr int kOffTRow = kOffCInfo + kCtxBufs * 16;
-    static constexpr int kOffInfo = kOffTRow + kTileRing * kTileM * 4;
+    static constexpr int kOffTInfo = kOffTRow + kTileRing * kTileM * 4;
+    static constexpr int kOffInfo = kOffTInfo + kTileRing * 4;
     static constexpr int kOffBar = kOffInfo + kMaxStages * 4;
     static constexpr int kOffMisc = kOffBar + kNumBars * 8;
     static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
@@ -133,13 +140,14 @@ __device__ __forceinline__ uint32_t sel4(uint32_t a, uint32_t b, uint32_t c, uin
     return w == 0 ? a : (w == 1 ? b : (w == 2 ? c : d));
 }
 
-template <int CI, int CO, typename T, bool FLIP, int NG>
+template <int CI, int CO, typename T, bool FLIP, int NG, bool SPLIT>
 __global__ void __launch_bounds__(TcRoles<NG>::kThreads, TcCfg<CI, CO>::kMinBlocks)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__ feats,
                const T *__restrict__ bias, const int32_t *__restrict__ nbr,
                const uint32_t *__restrict__ masks, const int32_t *__restrict__ order,
                T *__restrict__ out, int64_t M, int V, int MW, int MWS, int num_tiles, int row_mode,
-               int32_t *status, uint64_t wait_ns) {
+               int32_t *status, uint64_t wait_ns, int split_tiles, float *__restrict__ partials,
+               int *__restrict__ split_cnt) {
     using Cfg = TcCfg<CI, CO>;
     using Roles = TcRoles<NG>;
     constexpr int S = Cfg::kStages, KC = Cfg::KC, NKC = Cfg::NKC, RB = Cfg::kRowBytes;
@@ -157,6 +165,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     int32_t *s_act = reinterpret_cast<int32_t *>(base + Cfg::kOffAct);    // [ctx][i] -> v
     int4 *s_cinfo = reinterpret_cast<int4 *>(base + Cfg::kOffCInfo);      // [ctx] {k, cnt, flags}
     int32_t *s_trow = reinterpret_cast<int32_t *>(base + Cfg::kOffTRow);  // [tile % ring][row]
+    int32_t *s_tinfo = reinterpret_cast<int32_t *>(base + Cfg::kOffTInfo); // [tile % ring]: split slot*2+half, -1, end
     uint32_t *s_info = reinterpret_cast<uint32_t *>(base + Cfg::kOffInfo);
     uint64_t *bar = reinterpret_cast<uint64_t *>(base + Cfg::kOffBar);
     uint64_t *full = bar, *empty = bar + 8, *cfull = bar + 16, *cempty = bar + 19;
@@ -199,12 +208,19 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     grid_dependency_wait();                  // the map build's order, masks and map
 
     // Tiles are taken from the end of the voxel order first: voxels with the most neighbours
-    // sort last, so the tiles with the most active offsets start earliest. CTA c takes tiles
-    // c + kG (k >= 1) after a first tile G-1-c: the CTAs that get one tile fewer (the last
-    // round is partial) take the heaviest first tiles.
+    // sort last, so the tiles with the most active offsets start earliest. CTA c takes work
+    // items c + kG (k >= 1) after a first item G-1-c: the CTAs that get one item fewer (the last
+    // round is partial) take the heaviest first items. Item i is the tile of rank i (rank 0 =
+    // the last 128 voxels of the order); with SPLIT, the first split_tiles ranks have two items
+    // each (2r: the first half of the tile's active offsets, 2r+1: the second half), which run
+    // on different CTAs when the tile has more than kSplitMinAct active offsets.
     const int G = gridDim.x;
-    const int nt = (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    const int R = SPLIT ? split_tiles : 0;
+    const int n_items = num_tiles + R;
+    const int nt = (int)blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / G + 1 : 0;
     auto tile_id = [&](int k) { return k == 0 ? G - 1 - (int)blockIdx.x : (int)blockIdx.x + k * G; };
+    auto item_rank = [&](int item) { return item < 2 * R ? item >> 1 : item - R; };
+    auto item_half = [&](int item) { return item < 2 * R ? (item & 1) : -1; };
     const bool use_masks = MWS > 0;
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
         return mbar_wait_or_abort(smem_u32(b), parity, s_abort, wait_ns);
@@ -219,7 +235,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             for (int j = 0; j < 4; ++j) {
                 r[j] = -1;
                 if (k < nt) {
-                    const int64_t p = (int64_t)(num_tiles - 1 - tile_id(k)) * kTileM + 4 * lane + j;
+                    const int64_t p = (int64_t)(num_tiles - 1 - item_rank(tile_id(k))) * kTileM + 4 * lane + j;
                     if (p < M) r[j] = order ? __ldg(order + p) : (int32_t)p;
                 }
             }
@@ -251,6 +267,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             if (lane == 0) mbar_arrive(smem_u32(&cfull[pend]));
             pend = -1;
         };
+        int kt = 0;                          // tiles (non-empty items) handed to the MMA and epilogue
         for (int k = 0; k < nt && ok; ++k) {
             uint32_t tm[kMaxMaskWords];
             int nact = 0;
@@ -266,11 +283,29 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             }
             if (!use_masks) nact = V;
             const bool fake = nact == 0;     // no offset: one step of zeros gives the bias rows
-            int left = fake ? 1 : nact;
+            // This item's share of the tile's active offsets: [lo, hi).
+            int lo = 0, hi = nact, tinfo = -1;
+            bool skip = false;
+            if (SPLIT) {
+                const int item = tile_id(k), half = item_half(item);
+                if (half >= 0) {
+                    if (nact > kSplitMinAct) {
+                        const int h = (nact + 1) >> 1;
+                        if (half == 0) hi = h;
+                        else lo = h;
+                        tinfo = item_rank(item) * 2 + half;
+                    } else if (half == 1) {
+                        skip = true;         // a light tile runs whole as its first item
+                    }
+                }
+            }
+            if (!skip) {
+            int left = fake ? 1 : hi - lo;
 
-            const int t = k % kTileRing;
-            if (k >= kTileRing && !wait(&tempty[t], (uint32_t)(((k / kTileRing) - 1) & 1))) { ok = false; break; }
+            const int t = kt % kTileRing;
+            if (kt >= kTileRing && !wait(&tempty[t], (uint32_t)(((kt / kTileRing) - 1) & 1))) { ok = false; break; }
             *reinterpret_cast<int4 *>(&s_trow[t * kTileM + 4 * lane]) = make_int4(rA[0], rA[1], rA[2], rA[3]);
+            if (lane == 0) s_tinfo[t] = tinfo;
             {
                 int base_v = 0;
 #pragma unroll
@@ -290,9 +325,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tfull[t]));
 
-            int c0 = 0;                      // first active offset of the next context
+            int c0 = lo;                     // first active offset of the next context
             bool first = true;
-            if (Cfg::kRows && row_mode && nact >= kRowsMinAct) {
+            if (Cfg::kRows && row_mode && hi - lo >= kRowsMinAct) {
                 // One context per tile: stage every voxel's whole index row (V <= 28 words) as a
                 // 128-byte aligned window, 8 lanes per row, 16 bytes per lane. Chunk c of row r
                 // lands in slot (c + rot) % 8, rot = (r + r/8) % 8, so word j of the row sits at
@@ -301,7 +336,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 const int cb = g % kCtxBufs;
                 if (g >= kCtxBufs && !wait(&cempty[cb], (uint32_t)(((g / kCtxBufs) - 1) & 1))) { ok = false; break; }
                 const int cnt = left;
-                if (lane < cnt) s_act[cb * kActMax + lane] = fake ? 0 : (use_masks ? (int)s_tact[lane] : lane);
+                if (lane < cnt) s_act[cb * kActMax + lane] = fake ? 0 : (use_masks ? (int)s_tact[lo + lane] : lo + lane);
                 const char *nb = reinterpret_cast<const char *>(nbr);
                 const int64_t nbytes = M * (int64_t)V * 4;
                 const int c = lane & 7, rs = lane >> 3;
@@ -333,7 +368,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 }
                 cp_async_commit();
                 left = 0;
-                if (lane == 0) s_cinfo[cb] = make_int4(k, cnt, kCtxFirst | kCtxLast | kCtxRows, 0);
+                if (lane == 0) s_cinfo[cb] = make_int4(kt, cnt, kCtxFirst | kCtxLast | kCtxRows, 0);
                 publish_pending(false);      // the previous tile's rows have landed
                 pend = cb;
                 ++g;
@@ -373,14 +408,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 cp_async_commit();
                 c0 += cnt;
                 left -= cnt;
-                if (lane == 0) s_cinfo[cb] = make_int4(k, cnt, (first ? kCtxFirst : 0) | (left == 0 ? kCtxLast : 0), 0);
+                if (lane == 0) s_cinfo[cb] = make_int4(kt, cnt, (first ? kCtxFirst : 0) | (left == 0 ? kCtxLast : 0), 0);
                 first = false;
                 publish_pending(false);      // the previous context's loads have landed
                 pend = cb;
                 ++g;
             }
             if (!ok) break;
-            // next tile: rows of k+3 and masks of k+2 start loading now
+            ++kt;
+            }                                // !skip
+            // next item: rows of k+3 and masks of k+2 start loading now
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 rA[j] = rB[j];
@@ -392,7 +429,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             load_rows(k + 3, rC);
         }
         publish_pending(true);
-        if (ok) {                            // end marker
+        if (ok) {                            // end marker for the epilogue
+            const int t = kt % kTileRing;
+            if (kt < kTileRing || wait(&tempty[t], (uint32_t)(((kt / kTileRing) - 1) & 1))) {
+                if (lane == 0) s_tinfo[t] = kTileEnd;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tfull[t]));
+            } else {
+                ok = false;
+            }
+        }
+        if (ok) {                            // end marker for the gatherers and the MMA
             const int cb = g % kCtxBufs;
             if (g < kCtxBufs || wait(&cempty[cb], (uint32_t)(((g / kCtxBufs) - 1) & 1))) {
                 if (lane == 0) s_cinfo[cb] = make_int4(0, 0, kCtxEnd, 0);
@@ -561,37 +608,83 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
         // ------------------------------------------------------------------ epilogue
         constexpr int kCols = CO < 32 ? CO : 32;      // columns per TMEM load batch
         const int quad = warp & 3;
-        for (int k = 0; k < nt; ++k) {
+        for (int k = 0;; ++k) {
             const int b = k & 1, t = k % kTileRing;
-            if (!wait(&afull[b], (uint32_t)((k >> 1) & 1))) break;
             if (!wait(&tfull[t], (uint32_t)((k / kTileRing) & 1))) break;
+            const int tinfo = s_tinfo[t];
+            if (tinfo == kTileEnd) break;
+            if (!wait(&afull[b], (uint32_t)((k >> 1) & 1))) break;
             tc_fence_after();
             const int32_t row = s_trow[t * kTileM + quad * 32 + lane];
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tempty[t]));
             const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * CO);
             T *orow = out + (int64_t)(row < 0 ? 0 : row) * CO;
+            // Writes accumulator columns [c0, c0 + kCols) of this lane's row (+ `add`, + bias).
+            auto write_out = [&](int c0, const uint32_t (&acc)[kCols], const float *add) {
 #pragma unroll
-            for (int c0 = 0; c0 < CO; c0 += kCols) {
-                uint32_t acc[kCols];
+                for (int m = 0; m < kCols / 8; ++m) {
+                    float f[8];
 #pragma unroll
-                for (int m = 0; m < kCols / 8; ++m) tmem_ld8(taddr + c0 + m * 8, &acc[m * 8]);
-                tc_wait_ld();
-                if (row >= 0) {
+                    for (int q = 0; q < 8; ++q) {
+                        f[q] = __uint_as_float(acc[m * 8 + q]);
+                        if (add) f[q] += __ldcg(add + c0 + m * 8 + q);
+                        if (bias) f[q] += dtype_traits<T>::to_f(bias[c0 + m * 8 + q]);
+                    }
+                    uint4 p;
+                    p.x = pack2<T>(f[0], f[1]);
+                    p.y = pack2<T>(f[2], f[3]);
+                    p.z = pack2<T>(f[4], f[5]);
+                    p.w = pack2<T>(f[6], f[7]);
+                    *reinterpret_cast<uint4 *>(orow + c0 + m * 8) = p;
+                }
+            };
+            if (!SPLIT || tinfo < 0) {
 #pragma unroll
-                    for (int m = 0; m < kCols / 8; ++m) {
-                        float f[8];
+                for (int c0 = 0; c0 < CO; c0 += kCols) {
+                    uint32_t acc[kCols];
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            f[q] = __uint_as_float(acc[m * 8 + q]);
-                            if (bias) f[q] += dtype_traits<T>::to_f(bias[c0 + m * 8 + q]);
-                        }
-                        uint4 p;
-                        p.x = pack2<T>(f[0], f[1]);
-                        p.y = pack2<T>(f[2], f[3]);
-                        p.z = pack2<T>(f[4], f[5]);
-                        p.w = pack2<T>(f[6], f[7]);
-                        *reinterpret_cast<uint4 *>(orow + c0 + m * 8) = p;
+                    for (int m = 0; m < kCols / 8; ++m) tmem_ld8(taddr + c0 + m * 8, &acc[m * 8]);
+                    tc_wait_ld();
+                    if (row >= 0) write_out(c0, acc, nullptr);
+                }
+            } else {
+                // Half of a split tile: publish this half's fp32 partial rows, then count the
+                // halves done (per tile and lane quadrant); the second to finish adds the other
+                // half's partial (fp32 addition of two terms commutes, so the result does not
+                // depend on which half finishes last) and writes the output rows.
+                const int slot = tinfo >> 1, half = tinfo & 1;
+                const int64_t prow = (int64_t)quad * 32 + lane;
+                float *mine = partials + ((int64_t)(slot * 2 + half) * kTileM + prow) * CO;
+                const float *other = partials + ((int64_t)(slot * 2 + (half ^ 1)) * kTileM + prow) * CO;
+#pragma unroll
+                for (int c0 = 0; c0 < CO; c0 += kCols) {
+                    uint32_t acc[kCols];
+#pragma unroll
+                    for (int m = 0; m < kCols / 8; ++m) tmem_ld8(taddr + c0 + m * 8, &acc[m * 8]);
+                    tc_wait_ld();
+                    if (row >= 0) {
+#pragma unroll
+                        for (int m = 0; m < kCols / 4; ++m)
+                            __stcg(reinterpret_cast<float4 *>(mine + c0) + m,
+                                   make_float4(__uint_as_float(acc[4 * m]), __uint_as_float(acc[4 * m + 1]),
+                                               __uint_as_float(acc[4 * m + 2]), __uint_as_float(acc[4 * m + 3])));
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                int done = 0;
+                if (lane == 0) done = atomicAdd(split_cnt + slot * 4 + quad, 1);
+                done = __shfl_sync(0xffffffffu, done, 0);
+                if (done == 1) {
+                    __threadfence();
+#pragma unroll
+                    for (int c0 = 0; c0 < CO; c0 += kCols) {
+                        uint32_t acc[kCols];
+#pragma unroll
+                        for (int m = 0; m < kCols / 8; ++m) tmem_ld8(taddr + c0 + m * 8, &acc[m * 8]);
+                        tc_wait_ld();
+                        if (row >= 0) write_out(c0, acc, other);
                     }
                 }
             }
@@ -656,22 +749,61 @@ static bool make_tmap_2d(CUtensorMap *map, const void *ptr, uint64_t cols, uint6
     return true;
 }
 
-// Gatherer warps: eight where a CTA has an SM to itself (large stages), four where two CTAs
-// share one. Two gatherer warps per SM sub-partition keep more cp.async issue in flight than
-// one: a gatherer's step is a short dependent chain (index, address, copy, commit, wait).
+// Gatherer warps: four, whether a CTA has an SM to itself (large stages) or two CTAs share
+// one. Measured on B200 with the conv alone on cached maps: eight gatherer warps took the
+// indoor conv (C=64) from 875 to 901 us and sixteen to 1,015 us; wide3 / wide5 (C=128) were
+// unchanged with eight and 10-15 % slower with sixteen. More warps issuing cp.async do not
+// raise the gather rate, so it is not one warp's dependent chain that bounds it.
 #ifndef SPCONV_TC_GATHER_WARPS_1CTA
-#define SPCONV_TC_GATHER_WARPS_1CTA 8
+#define SPCONV_TC_GATHER_WARPS_1CTA 4
 #endif
 #ifndef SPCONV_TC_GATHER_WARPS_2CTA
 #define SPCONV_TC_GATHER_WARPS_2CTA 4
 #endif
 
-template <int CI, int CO, typename T, bool FLIP>
+// The weight's tensor map, encoded once per (device, address, shape): eager calls reuse it.
+// A map holds only the address, sizes, strides and box, so a later tensor at the same address
+// with the same shape is described by the same map.
+struct TmapKey {
+    int dev;
+    const void *ptr;
+    uint64_t cols, rows;
+    uint32_t box_cols;
+    bool operator==(const TmapKey &o) const {
+        return dev == o.dev && ptr == o.ptr && cols == o.cols && rows == o.rows && box_cols == o.box_cols;
+    }
+};
+
+static bool weight_tmap(CUtensorMap *map, int dev, const void *ptr, uint64_t cols, uint64_t rows,
+                        uint32_t box_cols, uint32_t box_rows) {
+    constexpr int kEntries = 32;
+    static std::mutex mu;
+    static TmapKey keys[kEntries];
+    static CUtensorMap maps[kEntries];
+    static int used = 0, next = 0;
+    const TmapKey key{dev, ptr, cols, rows, box_cols};
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        for (int i = 0; i < used; ++i)
+            if (keys[i] == key) {
+                *map = maps[i];
+                return true;
+            }
+    }
+    if (!make_tmap_2d(map, ptr, cols, rows, cols * 2, box_cols, box_rows)) return false;
+    std::lock_guard<std::mutex> lk(mu);
+    const int i = used < kEntries ? used++ : (next++ % kEntries);
+    keys[i] = key;
+    maps[i] = *map;
+    return true;
+}
+
+template <int CI, int CO, typename T, bool FLIP, bool SPLIT>
 static int launch_tc_k(const ConvArgs &a) {
     using Cfg = TcCfg<CI, CO>;
     constexpr int NG = Cfg::kMinBlocks >= 2 ? SPCONV_TC_GATHER_WARPS_2CTA : SPCONV_TC_GATHER_WARPS_1CTA;
     constexpr int kThreads = TcRoles<NG>::kThreads;
-    auto kern = conv_tc_kernel<CI, CO, T, FLIP, NG>;
+    auto kern = conv_tc_kernel<CI, CO, T, FLIP, NG, SPLIT>;
     const int MWS = (a.masks && a.MW <= kMaxMaskWords) ? a.MW : 0;
     // Shared memory is padded so that no more CTAs fit on an SM than its 512 TMEM columns
     // serve (228 KB of shared memory per SM, 1 KB reserved per CTA): tcgen05.alloc never waits.
@@ -700,26 +832,47 @@ static int launch_tc_k(const ConvArgs &a) {
     const int occ_dev = occ_cache[dev];
     attr_lock.unlock();
     CUtensorMap tw;
-    if (!make_tmap_2d(&tw, a.weight, (uint64_t)a.V * CI, (uint64_t)CO, (uint64_t)a.V * CI * 2, Cfg::KC, CO))
+    if (!weight_tmap(&tw, dev, a.weight, (uint64_t)a.V * CI, (uint64_t)CO, Cfg::KC, CO))
         return SPCONV_ERR_CUDA;
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int num_tiles = (int)((a.M + kTileM - 1) / kTileM);
+    int split_tiles = 0;
+    float *partials = nullptr;
+    int *split_cnt = nullptr;
+    if (SPLIT) {
+        split_tiles = num_tiles < kSplitMaxTiles ? num_tiles : kSplitMaxTiles;
+        split_cnt = reinterpret_cast<int *>(a.split_ws);
+        partials = reinterpret_cast<float *>(reinterpret_cast<char *>(a.split_ws) + split_counter_bytes());
+        if (cudaMemsetAsync(split_cnt, 0, (size_t)split_tiles * 4 * sizeof(int), a.stream) != cudaSuccess)
+            return check_launch("conv_tc: split counter memset");
+    }
     int grid = sms * occ_dev;
-    if (grid > num_tiles) grid = num_tiles;
+    if (grid > num_tiles + split_tiles) grid = num_tiles + split_tiles;
     if (grid < 1) grid = 1;
     // Whole index rows are staged when one fits a 128-byte window and the map is 16-byte aligned.
     const int row_mode = (a.V <= kRowsMaxV && ((uintptr_t)a.nbr & 15u) == 0) ? 1 : 0;
     const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(kThreads), (size_t)smem, a.stream, tw,
                                       (const T *)a.feats, (const T *)a.bias, a.nbr, a.masks, a.order, (T *)a.out,
-                                      a.M, a.V, a.MW, MWS, num_tiles, row_mode, a.status, wait_limit_ns());
+                                      a.M, a.V, a.MW, MWS, num_tiles, row_mode, a.status, wait_limit_ns(),
+                                      split_tiles, partials, split_cnt);
     if (le != cudaSuccess) return check_launch("conv_tc_kernel launch");
     return check_launch("conv_tc_kernel");
 }
 
 template <int CI, int CO, typename T>
 static int launch_tc(const ConvArgs &a) {
-    return a.flip ? launch_tc_k<CI, CO, T, true>(a) : launch_tc_k<CI, CO, T, false>(a);
+    if (a.flip) return launch_tc_k<CI, CO, T, true, false>(a);
+    if (a.split_ws) return launch_tc_k<CI, CO, T, false, true>(a);
+    return launch_tc_k<CI, CO, T, false, false>(a);
+}
+
+int64_t split_counter_bytes() { return ((int64_t)kSplitMaxTiles * 4 * 4 + 255) & ~int64_t(255); }
+
+int64_t conv_split_workspace_bytes(int64_t M, int Co) {
+    const int64_t tiles = (M + kTileM - 1) / kTileM;
+    const int64_t r = tiles < kSplitMaxTiles ? tiles : kSplitMaxTiles;
+    return split_counter_bytes() + r * 2 * kTileM * (int64_t)Co * 4;
 }
 
 bool tc_supported(int dtype, int Ci, int Co, int V) {

@@ -47,6 +47,10 @@ SIGNATURES = {
     "spconv_submanifold_conv_forward_ex": (_c_int, [
         _c_void_p, _c_int, _c_i64, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int]),
+    "spconv_conv_splitk_workspace_bytes": (_c_i64, [_c_i64, _c_int]),
+    "spconv_submanifold_conv_forward_splitk": (_c_int, [
+        _c_void_p, _c_int, _c_i64, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_i64, _c_void_p, _c_void_p, _c_void_p]),
     "spconv_build_submanifold_neighbor_map_noalloc": (_c_int, [
         _c_void_p, _c_i64, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
@@ -323,10 +327,13 @@ def build_neighbor_map_2d(coords: torch.Tensor, batch: int, W: int, H: int,
 
 def conv_forward(feats: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
                  nbr: torch.Tensor, masks: Optional[torch.Tensor], order: Optional[torch.Tensor],
-                 kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 kernel: int = KERNEL_AUTO, out: Optional[torch.Tensor] = None,
+                 split: bool = False) -> torch.Tensor:
     """out[i] = bias + sum_v feats[nbr[i,v]] @ weight[:, v, :]^T over valid neighbours.
 
-    ``weight`` is [Co, V, Ci] (or [Co, Kw, Kh, Kd, Ci]) in the dtype of ``feats``.
+    ``weight`` is [Co, V, Ci] (or [Co, Kw, Kh, Kd, Ci]) in the dtype of ``feats``. ``split``
+    runs the split-K variant (``spconv_submanifold_conv_forward_splitk``: the heaviest tiles'
+    offsets spread over two CTAs, fp32 partials in a workspace from torch's allocator).
     """
     lib = load_library()
     dev = _require_cuda(feats, weight, bias, nbr, masks, order)
@@ -367,6 +374,17 @@ def conv_forward(feats: torch.Tensor, weight: torch.Tensor, bias: Optional[torch
         return out
     before_launch(dev)
     st = status_word(dev)
+    if split:
+        need = int(lib.spconv_conv_splitk_workspace_bytes(M, Co))
+        ws = torch.empty((need,), dtype=torch.uint8, device=dev)
+        rc = lib.spconv_submanifold_conv_forward_splitk(
+            feats.data_ptr(), DTYPE_CODES[feats.dtype], M, Ci, w.data_ptr(),
+            None if b is None else b.data_ptr(), Co, V, nb.data_ptr(),
+            None if mk is None else mk.data_ptr(), None if od is None else od.data_ptr(),
+            ws.data_ptr(), need, out.data_ptr(), st.word.data_ptr(), _stream_ptr(dev))
+        if rc != SPCONV_OK:
+            _raise(rc, "spconv_submanifold_conv_forward_splitk")
+        return out
     rc = lib.spconv_submanifold_conv_forward_ex(
         feats.data_ptr(), DTYPE_CODES[feats.dtype], M, Ci, w.data_ptr(),
         None if b is None else b.data_ptr(), Co, V, nb.data_ptr(),

@@ -115,7 +115,9 @@ class SubMConv3dFunction(Function):
         bias: Optional[torch.Tensor] = None,
         algorithm: str = Algorithm.EXPLICIT_GEMM,
     ) -> torch.Tensor:
-        """Conv over a built map (ops:63-103); every algorithm runs the CUDA kernels."""
+        """Conv over a built map (ops:63-103); every algorithm runs the CUDA kernels. The two
+        split-K values (empty slots in the reference, ops:94-99) run the split-K variant, which
+        spreads the heaviest tiles' offsets over two CTAs; the others run the unsplit kernel."""
         assert feats.is_contiguous(), "Input features should be contiguous."
         if algorithm not in _ALGORITHMS:
             raise ValueError(f"Unsupported Algorithm {algorithm}.")
@@ -124,7 +126,8 @@ class SubMConv3dFunction(Function):
         if nbr.shape[1] != Kw * Kh * Kd:
             raise ValueError(
                 f"neighbor map has {nbr.shape[1]} offsets, weight has {Kw * Kh * Kd}")
-        out = _native.conv_forward(feats, weight, bias, nbr, masks, order)
+        split = algorithm in (Algorithm.IMPLICIT_GEMM_SPLITK, Algorithm.MASKED_IMPLICIT_GEMM_SPLITK)
+        out = _native.conv_forward(feats, weight, bias, nbr, masks, order, split=split)
         _native.after_launch(out.device)
         return out
 
