@@ -160,14 +160,19 @@ __device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait for the phase with the given parity to complete. Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t addr, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t addr, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         if (mbar_try_wait(addr, parity)) return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
+// Clean-up bound of an abandoned kernel waiting for its own weight-tile TMA loads: their
+// barrier phase may never complete (a gatherer that gave up does not arrive), and a load of a
+// few KB from L2/HBM lands within microseconds, so 200 us covers it with a wide margin.
+constexpr uint64_t kTmaDrainNs = 200000ull;
 
 __device__ __forceinline__ void mbar_arrive(uint32_t addr) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n"

@@ -18,7 +18,7 @@
 //             swizzled K-major layout; a step is signalled on the stage's "full" mbarrier once
 //             its copies have landed (cp.async.wait_group, proxy fence, arrive), D-1 steps
 //             behind the issue, so several steps per warp are in flight; warp 1 lane 0 also
-//             loads W[:, v, kc] into the B stage by TMA, counted on the stage's "wfull" mbarrier;
+//             loads W[:, v, kc] into the B stage by TMA (bytes counted on the same mbarrier);
 //   warp NG+1 MMA: one thread waits for a full stage (rows and weights), issues KC/16
 //             tcgen05.mma (M=128, N=Co, K=16) into the tile's TMEM accumulator, and commits to
 //             the stage's "empty" mbarrier (and, after a tile's last step, to the accumulator's);
@@ -48,8 +48,8 @@ constexpr int kCtxBufs = 3;
 constexpr int kTileRing = 4;        // tiles whose rows the epilogue may still need
 constexpr int kMaxMaskWords = 4;    // offset masks are used for V <= 128 (else all offsets run)
 constexpr int kMaxStages = 8;
-// mbarriers: full[8] empty[8] cfull[3] cempty[3] afull[2] aempty[2] tfull[4] tempty[4] wfull[8]
-constexpr int kNumBars = 42;
+// mbarriers: full[8] empty[8] cfull[3] cempty[3] afull[2] aempty[2] tfull[4] tempty[4]
+constexpr int kNumBars = 34;
 // Warp roles for NG gatherer warps: scheduler 0, gatherers 1..NG, MMA NG+1, epilogue NG+2..NG+5.
 constexpr int kWarpSched = 0, kWarpGather = 1;
 template <int NG> struct TcRoles {
@@ -170,16 +170,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     uint64_t *bar = reinterpret_cast<uint64_t *>(base + Cfg::kOffBar);
     uint64_t *full = bar, *empty = bar + 8, *cfull = bar + 16, *cempty = bar + 19;
     uint64_t *afull = bar + 22, *aempty = bar + 24, *tfull = bar + 26, *tempty = bar + 30;
-    uint64_t *wfull = bar + 34;    // per stage: the weight tile's TMA bytes (and the step info)
     uint32_t *s_tmem = reinterpret_cast<uint32_t *>(base + Cfg::kOffMisc);
     volatile int *s_abort = reinterpret_cast<volatile int *>(base + Cfg::kOffMisc + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(&full[s]), NG);
+            mbar_init(smem_u32(&full[s]), NG + 1);
             mbar_init(smem_u32(&empty[s]), 1);
-            mbar_init(smem_u32(&wfull[s]), 1);
         }
         for (int c = 0; c < kCtxBufs; ++c) {
             mbar_init(smem_u32(&cfull[c]), 1);
@@ -429,7 +427,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             load_rows(k + 3, rC);
         }
         publish_pending(true);
-        if (ok) {                            // end marker for the epilogue
+        if (SPLIT && ok) {                   // end marker for the epilogue (item count varies)
             const int t = kt % kTileRing;
             if (kt < kTileRing || wait(&tempty[t], (uint32_t)(((kt / kTileRing) - 1) & 1))) {
                 if (lane == 0) s_tinfo[t] = kTileEnd;
@@ -519,8 +517,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                     if (b_loader) {
                         s_info[s] = (uint32_t)k | ((cfirst && i == 0 && kc == 0) ? kInfoFirst : 0u) |
                                     ((clast && i == cnt - 1 && kc == NKC - 1) ? kInfoLast : 0u);
-                        mbar_arrive_expect_tx(smem_u32(&wfull[s]), (uint32_t)Cfg::kBBytes);
-                        tma_load_2d(sB + s * Cfg::kBBytes, &tmap_w, v * CI + kc * KC, 0, smem_u32(&wfull[s]));
+                        mbar_arrive_expect_tx(smem_u32(&full[s]), (uint32_t)Cfg::kBBytes);
+                        tma_load_2d(sB + s * Cfg::kBBytes, &tmap_w, v * CI + kc * KC, 0, smem_u32(&full[s]));
                     }
                     const uint32_t a_st = sA + s * Cfg::kABytes;
                     const T *src = feats + kc * KC + chunk * 8;
@@ -550,7 +548,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             if (u == 0 || wait(&empty[s], (uint32_t)((u - 1) & 1))) {
                 if (b_loader) {
                     s_info[s] = kInfoEnd;
-                    mbar_arrive(smem_u32(&wfull[s]));
+                    mbar_arrive(smem_u32(&full[s]));
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&full[s]));
@@ -558,11 +556,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
         }
         cp_async_wait_all();
         if (!ok && b_loader) {
-            // wait (bounded) for the weight loads of the last step issued on each stage; each
-            // has a barrier of its own, so these waits end as soon as the bytes have landed
+            // wait (bounded) for the weight loads of the last step issued on each stage: the
+            // stage's phase completes once its bytes have landed, unless a gatherer that gave
+            // up never arrives on it; then kTmaDrainNs bounds the wait
             for (int q = 1; q <= S && q <= step; ++q) {
                 const int st = step - q;
-                mbar_wait_bounded(smem_u32(&wfull[st % S]), (uint32_t)((st / S) & 1));
+                mbar_wait_bounded(smem_u32(&full[st % S]), (uint32_t)((st / S) & 1), kTmaDrainNs);
             }
         }
     } else if (warp == kWarpMma) {
@@ -573,8 +572,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             int acc0 = 0, acc1 = 0;          // commits made to afull[0], afull[1]
             for (;;) {
                 const int s = step % S, u = step / S;
-                if (!wait(&full[s], (uint32_t)(u & 1))) break;       // the A rows
-                if (!wait(&wfull[s], (uint32_t)(u & 1))) break;      // the weight tile, the step info
+                if (!wait(&full[s], (uint32_t)(u & 1))) break;
                 const uint32_t info = s_info[s];
                 if (info == kInfoEnd) break;
                 const int k = (int)(info & 0x3fffffffu);
@@ -608,12 +606,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
         // ------------------------------------------------------------------ epilogue
         constexpr int kCols = CO < 32 ? CO : 32;      // columns per TMEM load batch
         const int quad = warp & 3;
-        for (int k = 0;; ++k) {
+        for (int k = 0; SPLIT || k < nt; ++k) {
             const int b = k & 1, t = k % kTileRing;
-            if (!wait(&tfull[t], (uint32_t)((k / kTileRing) & 1))) break;
-            const int tinfo = s_tinfo[t];
-            if (tinfo == kTileEnd) break;
-            if (!wait(&afull[b], (uint32_t)((k >> 1) & 1))) break;
+            int tinfo = -1;
+            if (SPLIT) {     // items without work publish no tile: the scheduler marks the end
+                if (!wait(&tfull[t], (uint32_t)((k / kTileRing) & 1))) break;
+                tinfo = s_tinfo[t];
+                if (tinfo == kTileEnd) break;
+                if (!wait(&afull[b], (uint32_t)((k >> 1) & 1))) break;
+            } else {
+                if (!wait(&afull[b], (uint32_t)((k >> 1) & 1))) break;
+                if (!wait(&tfull[t], (uint32_t)((k / kTileRing) & 1))) break;
+            }
             tc_fence_after();
             const int32_t row = s_trow[t * kTileM + quad * 32 + lane];
             __syncwarp();
