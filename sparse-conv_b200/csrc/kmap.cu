@@ -67,7 +67,7 @@ struct WsLayout {
     int64_t cap = 0;
     bool key64 = false;
     int64_t bitmap_words = 0;
-    int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, total = 0;
+    int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, flags = 0, total = 0;
     int sort_tiles = 0;            // > 0: room for the radix-sort order (keys alias the table)
     int64_t sort_counts = 0;       // [kSortMaxPasses][256][sort_tiles] + [kSortMaxPasses][256] totals
 };
@@ -117,6 +117,7 @@ static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
     if (L.bitmap_words) { L.bitmap = off; off += align256(L.bitmap_words * 4); }
     L.hist = off; off += align256(kOrderBuckets * 4);
     L.cursor = off; off += align256(kOrderBuckets * 4);
+    L.flags = off; off += 256;          // per-call flags, cleared with the rest (word 0: duplicate seen)
     if (M >= kSortMinVoxels) {
         // Sort keys and values (4 x M words) reuse the table, dead once the map is built:
         // its capacity is at least 2M slots of 8 bytes.
@@ -170,7 +171,7 @@ __device__ __forceinline__ uint64_t home_group(uint64_t flat, uint64_t gmask, ui
 template <bool KEY64>
 __device__ __forceinline__ bool table_insert(unsigned long long *table, uint32_t *vals,
                                              uint64_t gmask, uint32_t shift, uint64_t flat,
-                                             uint32_t row, int32_t *status) {
+                                             uint32_t row, int32_t *status, int32_t *dup_flag) {
     const unsigned long long desired =
         KEY64 ? ~(unsigned long long)flat : ~((((unsigned long long)(uint32_t)flat) << 32) | row);
     uint64_t g = home_group<KEY64>(flat, gmask, shift);
@@ -191,6 +192,7 @@ __device__ __forceinline__ bool table_insert(unsigned long long *table, uint32_t
                 if (KEY64) atomicMax(vals + g * kGroup + i, row);
                 else atomicMin(grp + i, desired);        // min of the complement = max row
                 raise_status(status, SPCONV_STATUS_DUPLICATE);
+                *dup_flag = 1;                           // this call's own record of it
                 return true;
             }
         }
@@ -239,7 +241,7 @@ template <bool KEY64>
 __global__ void __launch_bounds__(256)
 insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, int D,
               unsigned long long *table, uint32_t *vals, uint32_t *bitmap, uint64_t gmask,
-              uint32_t shift, int32_t *status) {
+              uint32_t shift, int32_t *status, int32_t *dup_flag) {
     grid_launch_dependents();                                   // the map kernel's setup overlaps this
     const int lane = threadIdx.x & 31;
     // Whole warps iterate together (the bitmap update below shuffles across the warp).
@@ -270,7 +272,7 @@ insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, i
             const uint32_t pw = __shfl_up_sync(0xffffffffu, wi, 1);
             if (ok && (lane == 0 || pw != wi)) atomicOr(bitmap + wi, bits);
         }
-        if (ok && !table_insert<KEY64>(table, vals, gmask, shift, flat, (uint32_t)i, status))
+        if (ok && !table_insert<KEY64>(table, vals, gmask, shift, flat, (uint32_t)i, status, dup_flag))
             raise_status(status, SPCONV_STATUS_TABLE_FULL);
     }
 }
@@ -566,7 +568,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
               uint32_t *__restrict__ masks, uint32_t *hist,
-              int32_t *status) {
+              int32_t *status, const int32_t *dup_flag) {
     constexpr int V = 27;
     __shared__ uint32_t s_hist[kOrderBuckets];
     __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
@@ -646,10 +648,10 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     if (valid) s_stage[tid * V + V / 2] = (int32_t)i;
 
     // Sorted input keeps a voxel's z - Dd and z + Dd neighbours in the adjacent rows. With
-    // unique coordinates (the insert found no duplicate) a row holding that coordinate is the
-    // neighbour, so those offsets need no probe; otherwise they are probed as usual.
-    if (valid && (cand & ((1u << (V / 2 - 1)) | (1u << (V / 2 + 1)))) && status != nullptr &&
-        (*reinterpret_cast<volatile int32_t *>(status) & SPCONV_STATUS_DUPLICATE) == 0) {
+    // unique coordinates (this call's insert found no duplicate: a flag in its own workspace,
+    // so neither an earlier call nor another stream's affects it) a row holding that
+    // coordinate is the neighbour, so those offsets need no probe; otherwise they are probed.
+    if (valid && (cand & ((1u << (V / 2 - 1)) | (1u << (V / 2 + 1)))) && *dup_flag == 0) {
         if ((cand >> (V / 2 + 1)) & 1u) {
             if (i + 1 < M) {
                 const int4 n = __ldg(coords + i + 1);
@@ -1272,6 +1274,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     uint32_t *bitmap = L.bitmap_words ? (uint32_t *)(ws + L.bitmap) : nullptr;
     uint32_t *hist = (uint32_t *)(ws + L.hist);
     uint32_t *cursor = (uint32_t *)(ws + L.cursor);
+    int32_t *dup_flag = (int32_t *)(ws + L.flags);
     const uint64_t gmask = (uint64_t)(L.cap / kGroup) - 1;
     uint32_t shift = 32;
     for (int64_t c = L.cap / kGroup; c > 1; c >>= 1) --shift;   // 32 - log2(groups)
@@ -1289,9 +1292,9 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     const int ins_grid = (int)(gi < 65535LL * 32 ? gi : 65535LL * 32);
     stage_mark(SPCONV_STAGE_INSERT, 0, stream);
     if (key64)
-        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status);
+        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag);
     else
-        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status);
+        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag);
     if (int rc = check_launch("insert_kernel")) return rc;
     stage_mark(SPCONV_STAGE_INSERT, 1, stream);
 
@@ -1302,7 +1305,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
         launch_pdl(k3_fn, dim3(grid), dim3(kMapK3Threads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, (const unsigned long long *)table,
                    (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
-                   status);
+                   status, (const int32_t *)dup_flag);
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
         const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
@@ -1391,12 +1394,12 @@ namespace spconv {
 constexpr int64_t noalloc_capacity() { return capacity_for((int64_t)SPCONV_NOALLOC_MAX_COORDS); }
 constexpr int64_t align256c(int64_t x) { return (x + 255) & ~int64_t(255); }
 // The largest layout ws_layout gives for at most SPCONV_NOALLOC_MAX_COORDS voxels: 64-bit keys
-// (table + row array), no bitmap, histogram and cursors. The radix-sort counts are absent
+// (table + row array), no bitmap, histogram, cursors and the per-call flags. The radix-sort counts are absent
 // because such inputs stay below kSortMinVoxels (checked below); a 32-bit-key layout is smaller,
 // and its bitmap is dropped when it does not fit.
 constexpr int64_t kNoAllocScratchBytes =
     align256c(noalloc_capacity() * 8) + align256c(noalloc_capacity() * 4) +
-    2 * align256c(kOrderBuckets * 4) + 256;
+    2 * align256c(kOrderBuckets * 4) + 256 /* per-call flags */ + 256;
 static_assert((int64_t)SPCONV_NOALLOC_MAX_COORDS < kSortMinVoxels,
               "the no-alloc scratch has no room for the radix-sort counts: raise "
               "kNoAllocScratchBytes to cover ws_layout's sort_counts before raising the limit");

@@ -102,6 +102,22 @@ def test_duplicate_coordinates_keep_highest_row():
     _native.reset_status()
 
 
+def test_duplicate_next_to_its_z_neighbour_uses_the_highest_row():
+    """Sorted input whose z + 1 neighbour repeats: the adjacent row holds that coordinate but is
+    not the highest row of it, so the map build must probe (its own record of the duplicate,
+    kept in the call's workspace) rather than take the adjacent row. Repeated with the device
+    status word already holding a duplicate from an earlier call and after a clean call."""
+    dup = np.array([[0, 1, 1, 1], [0, 1, 1, 2], [0, 1, 1, 2], [0, 1, 2, 1]], dtype=np.int32)
+    clean = np.array([[0, 1, 1, 1], [0, 1, 1, 2], [0, 1, 2, 1]], dtype=np.int32)
+    shape = (1, 1, 5, 5, 5)
+    _native.reset_status()
+    for coords in (dup, dup, clean, dup):
+        nbr, _, _ = gpu_map(coords, shape, (3, 3, 3), (1, 1, 1))
+        np.testing.assert_array_equal(nbr, oracle.neighbor_map(coords, shape, (3, 3, 3)))
+    assert _native.check_errors(torch.device("cuda", 0)) & _native.STATUS_DUPLICATE
+    _native.reset_status()
+
+
 def test_out_of_range_coordinates_raise():
     coords = torch.tensor([[0, 1, 1, 1], [0, 5, 1, 1]], dtype=torch.int32, device="cuda")
     _native.reset_status()
