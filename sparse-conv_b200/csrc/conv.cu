@@ -2,36 +2,108 @@
 //
 // The SIMT kernel covers what the tcgen05 kernel does not: fp32 features (computed with
 // fp32 FMAs, not TF32, so results stay within 1e-4 of a float64 evaluation) and channel
-// counts outside {16, 32, 64, 128}. One thread computes one output element
+// counts outside {16, 32, 64, 128}:
 //   out[i, co] = bias[co] + sum_v sum_ci feats[nbr[i,v], ci] * weight[co, v, ci]
-// over the valid neighbours of row i, accumulating in fp32 and rounding once.
+// accumulated in fp32 (offsets ascending, then channels ascending) and rounded once.
+//
+// A block computes a tile of 64 consecutive entries of the voxel order x 32 output channels.
+// It ORs the tile's offset masks and walks only the offsets some row of the tile has; per
+// offset it gathers the 64 neighbour rows into shared memory in chunks of 32 input channels
+// (missing neighbours as zeros), stages W[co0 .. co0+31, v, chunk], and each thread
+// accumulates 2 rows x 4 output channels with fp32 FMAs.
 #include "common.cuh"
 #include "conv_internal.h"
 
 namespace spconv {
 
+constexpr int kSimtBM = 64, kSimtBN = 32, kSimtBK = 32, kSimtThreads = 256, kSimtMaxMW = 32;
+
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kSimtThreads)
 conv_simt_kernel(const T *__restrict__ feats, const T *__restrict__ weight,
                  const T *__restrict__ bias, const int32_t *__restrict__ nbr,
-                 int64_t M, int Ci, int Co, int V, int flip, T *__restrict__ out) {
-    const int64_t total = M * (int64_t)Co;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = idx / Co;
-        const int co = (int)(idx - row * Co);
-        const int32_t *nr = nbr + row * V;
-        float acc = 0.0f;
-        for (int v = 0; v < V; ++v) {
-            const int32_t n = __ldg(nr + (flip ? V - 1 - v : v));
-            if (n < 0 || n >= M) continue;       // rows outside the feature table read as missing
-            const T *f = feats + (int64_t)n * Ci;
-            const T *w = weight + ((int64_t)co * V + v) * Ci;
-            for (int ci = 0; ci < Ci; ++ci)
-                acc = fmaf(dtype_traits<T>::to_f(__ldg(f + ci)), dtype_traits<T>::to_f(__ldg(w + ci)), acc);
+                 const uint32_t *__restrict__ masks, const int32_t *__restrict__ order,
+                 int64_t M, int Ci, int Co, int V, int MW, int MWS, int flip, T *__restrict__ out) {
+    __shared__ float sA[kSimtBK][kSimtBM + 1];                  // [channel][row]
+    __shared__ __align__(16) float sB[kSimtBK][kSimtBN + 4];    // [channel][output channel]
+    __shared__ int32_t s_row[kSimtBM], s_nb[kSimtBM];
+    __shared__ uint32_t s_or[kSimtMaxMW];
+    const int tid = threadIdx.x;
+    const int64_t p0 = (int64_t)blockIdx.x * kSimtBM;
+    const int co0 = blockIdx.y * kSimtBN;
+    if (tid < kSimtBM) {
+        const int64_t p = p0 + tid;
+        int32_t r = -1;
+        if (p < M) {
+            r = order ? __ldg(order + p) : (int32_t)p;
+            if ((uint32_t)r >= (uint32_t)M) r = -1;            // order entries outside the table are ignored
         }
-        if (bias) acc += dtype_traits<T>::to_f(__ldg(bias + co));
-        out[idx] = dtype_traits<T>::from_f(acc);
+        s_row[tid] = r;
+    }
+    if (tid < kSimtMaxMW) s_or[tid] = 0u;
+    __syncthreads();
+    if (MWS > 0 && tid < kSimtBM && s_row[tid] >= 0)
+        for (int w = 0; w < MWS; ++w) atomicOr(&s_or[w], __ldg(masks + (int64_t)s_row[tid] * MW + w));
+    __syncthreads();
+    const int tr = tid >> 3, tc = tid & 7;                      // rows 2tr, 2tr+1; channels 4tc .. 4tc+3
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int v = 0; v < V; ++v) {
+        const int col = flip ? V - 1 - v : v;                   // the map column read for offset v
+        if (MWS > 0 && !((s_or[col >> 5] >> (col & 31)) & 1u)) continue;   // no row of the tile has it
+        if (tid < kSimtBM) {
+            const int32_t r = s_row[tid];
+            int32_t n = -1;
+            if (r >= 0) {
+                n = __ldg(nbr + (int64_t)r * V + col);
+                if ((uint32_t)n >= (uint32_t)M) n = -1;         // rows outside the feature table read as missing
+            }
+            s_nb[tid] = n;
+        }
+        __syncthreads();
+        for (int kc = 0; kc < Ci; kc += kSimtBK) {
+            for (int e = tid; e < kSimtBM * kSimtBK; e += kSimtThreads) {
+                const int r = e / kSimtBK, k = e - r * kSimtBK;
+                const int32_t n = s_nb[r];
+                float x = 0.f;
+                if (n >= 0 && kc + k < Ci) x = dtype_traits<T>::to_f(__ldg(feats + (int64_t)n * Ci + kc + k));
+                sA[k][r] = x;
+            }
+            for (int e = tid; e < kSimtBN * kSimtBK; e += kSimtThreads) {
+                const int k = e / kSimtBN, c = e - k * kSimtBN;
+                float x = 0.f;
+                if (co0 + c < Co && kc + k < Ci)
+                    x = dtype_traits<T>::to_f(__ldg(weight + ((int64_t)(co0 + c) * V + v) * Ci + kc + k));
+                sB[k][c] = x;
+            }
+            __syncthreads();
+            const int kmax = Ci - kc < kSimtBK ? Ci - kc : kSimtBK;
+            for (int k = 0; k < kmax; ++k) {
+                const float a0 = sA[k][2 * tr], a1 = sA[k][2 * tr + 1];
+                const float4 b = *reinterpret_cast<const float4 *>(&sB[k][4 * tc]);
+                acc[0][0] = fmaf(a0, b.x, acc[0][0]);
+                acc[0][1] = fmaf(a0, b.y, acc[0][1]);
+                acc[0][2] = fmaf(a0, b.z, acc[0][2]);
+                acc[0][3] = fmaf(a0, b.w, acc[0][3]);
+                acc[1][0] = fmaf(a1, b.x, acc[1][0]);
+                acc[1][1] = fmaf(a1, b.y, acc[1][1]);
+                acc[1][2] = fmaf(a1, b.z, acc[1][2]);
+                acc[1][3] = fmaf(a1, b.w, acc[1][3]);
+            }
+            __syncthreads();
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int32_t r = s_row[2 * tr + i];
+        if (r < 0) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int co = co0 + 4 * tc + j;
+            if (co >= Co) continue;
+            float f = acc[i][j];
+            if (bias) f += dtype_traits<T>::to_f(__ldg(bias + co));
+            out[(int64_t)r * Co + co] = dtype_traits<T>::from_f(f);
+        }
     }
 }
 
@@ -59,25 +131,26 @@ int occupancy_per_sm(const void *kern, int threads, int smem_dynamic) {
 }
 
 int launch_conv_simt(const ConvArgs &a) {
-    const int64_t total = a.M * (int64_t)a.Co;
-    int64_t blocks = (total + 255) / 256;
-    if (blocks > 148LL * 64) blocks = 148LL * 64;
-    if (blocks < 1) blocks = 1;
+    const int64_t tiles = (a.M + kSimtBM - 1) / kSimtBM;
+    SPCONV_REQUIRE(tiles <= 0x7fffffffLL, SPCONV_ERR_ARG, "too many rows for the SIMT conv");
+    const dim3 grid((unsigned)tiles, (unsigned)((a.Co + kSimtBN - 1) / kSimtBN));
+    const int MWS = (a.masks && a.MW <= kSimtMaxMW) ? a.MW : 0;
     switch (a.dtype) {
         case SPCONV_F32:
-            conv_simt_kernel<float><<<(int)blocks, 256, 0, a.stream>>>(
-                (const float *)a.feats, (const float *)a.weight, (const float *)a.bias, a.nbr,
-                a.M, a.Ci, a.Co, a.V, a.flip, (float *)a.out);
+            conv_simt_kernel<float><<<grid, kSimtThreads, 0, a.stream>>>(
+                (const float *)a.feats, (const float *)a.weight, (const float *)a.bias, a.nbr, a.masks, a.order,
+                a.M, a.Ci, a.Co, a.V, a.MW, MWS, a.flip, (float *)a.out);
             break;
         case SPCONV_F16:
-            conv_simt_kernel<__half><<<(int)blocks, 256, 0, a.stream>>>(
-                (const __half *)a.feats, (const __half *)a.weight, (const __half *)a.bias, a.nbr,
-                a.M, a.Ci, a.Co, a.V, a.flip, (__half *)a.out);
+            conv_simt_kernel<__half><<<grid, kSimtThreads, 0, a.stream>>>(
+                (const __half *)a.feats, (const __half *)a.weight, (const __half *)a.bias, a.nbr, a.masks, a.order,
+                a.M, a.Ci, a.Co, a.V, a.MW, MWS, a.flip, (__half *)a.out);
             break;
         case SPCONV_BF16:
-            conv_simt_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, a.stream>>>(
+            conv_simt_kernel<__nv_bfloat16><<<grid, kSimtThreads, 0, a.stream>>>(
                 (const __nv_bfloat16 *)a.feats, (const __nv_bfloat16 *)a.weight,
-                (const __nv_bfloat16 *)a.bias, a.nbr, a.M, a.Ci, a.Co, a.V, a.flip, (__nv_bfloat16 *)a.out);
+                (const __nv_bfloat16 *)a.bias, a.nbr, a.masks, a.order, a.M, a.Ci, a.Co, a.V, a.MW, MWS, a.flip,
+                (__nv_bfloat16 *)a.out);
             break;
         default:
             set_error("unsupported dtype code %d", a.dtype);

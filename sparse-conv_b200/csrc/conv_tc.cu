@@ -44,12 +44,20 @@ constexpr int kNPitch = kChunk + 1; // words per row in a context buffer (confli
 constexpr int kRowWindow = 32;      // words per staged index row: a 128-byte aligned window
 constexpr int kRowsMaxV = 28;       // V for which a voxel's whole index row fits one window
 constexpr int kActMax = 32;         // active offsets per context buffer
-constexpr int kCtxBufs = 3;
+// Index-context buffers (how far the scheduler may run ahead of the gatherers), by launch
+// shape. Measured on B200, conv alone on cached maps: one CTA per SM, 3 -> 4 -> 5 buffers took
+// the indoor conv (C=64) from 843 to 810 to 792 us (wide5, C=128: 851 -> 840 us); a sixth
+// would cost a pipeline stage. Two CTAs per SM (cube, C=32): 4 buffers 32.1 -> 31.1 us, 5 lose
+// occupancy (38 us).
+#ifndef SPCONV_TC_CTX_BUFS_1CTA
+#define SPCONV_TC_CTX_BUFS_1CTA 5
+#endif
+#ifndef SPCONV_TC_CTX_BUFS_2CTA
+#define SPCONV_TC_CTX_BUFS_2CTA 4
+#endif
 constexpr int kTileRing = 4;        // tiles whose rows the epilogue may still need
 constexpr int kMaxMaskWords = 4;    // offset masks are used for V <= 128 (else all offsets run)
 constexpr int kMaxStages = 8;
-// mbarriers: full[8] empty[8] cfull[3] cempty[3] afull[2] aempty[2] tfull[4] tempty[4]
-constexpr int kNumBars = 34;
 // Warp roles for NG gatherer warps: scheduler 0, gatherers 1..NG, MMA NG+1, epilogue NG+2..NG+5.
 constexpr int kWarpSched = 0, kWarpGather = 1;
 template <int NG> struct TcRoles {
@@ -81,6 +89,9 @@ struct TcCfg {
     // Whole-row staging pays where the gatherers are fast relative to the index loads (rows of
     // at most 64 bytes); wider rows keep the smaller per-offset buffers and one more stage.
     static constexpr bool kRows = KC <= 32;
+    static constexpr int kCtxBufs = kABytes + kBBytes <= 12 * 1024 ? SPCONV_TC_CTX_BUFS_2CTA : SPCONV_TC_CTX_BUFS_1CTA;
+    // mbarriers: full[8] empty[8] cfull[ctx] cempty[ctx] afull[2] aempty[2] tfull[ring] tempty[ring]
+    static constexpr int kNumBars = 16 + 2 * kCtxBufs + 4 + 2 * kTileRing;
     static constexpr int kBufWords = kTileM * (kRows ? kRowWindow : kNPitch);   // one context buffer
     static constexpr int kNBytes = kCtxBufs * kBufWords * 4;
     static_assert(kRowWindow >= kNPitch, "context buffer");
@@ -151,7 +162,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     using Cfg = TcCfg<CI, CO>;
     using Roles = TcRoles<NG>;
     constexpr int S = Cfg::kStages, KC = Cfg::KC, NKC = Cfg::NKC, RB = Cfg::kRowBytes;
-    constexpr int LPR = Cfg::kLanesPerRow, D = Cfg::kDepth;
+    constexpr int LPR = Cfg::kLanesPerRow, D = Cfg::kDepth, kCtxBufs = Cfg::kCtxBufs;
     constexpr int kWarpMma = Roles::kWarpMma, kWarpEpi = Roles::kWarpEpi, RPW = Roles::kRowsPerWarp;
     // rows per lane: each warp instruction moves 32 / LPR whole rows, NQ instructions per step
     constexpr int NQ = RPW * LPR / 32;
@@ -168,8 +179,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
     int32_t *s_tinfo = reinterpret_cast<int32_t *>(base + Cfg::kOffTInfo); // [tile % ring]: split slot*2+half, -1, end
     uint32_t *s_info = reinterpret_cast<uint32_t *>(base + Cfg::kOffInfo);
     uint64_t *bar = reinterpret_cast<uint64_t *>(base + Cfg::kOffBar);
-    uint64_t *full = bar, *empty = bar + 8, *cfull = bar + 16, *cempty = bar + 19;
-    uint64_t *afull = bar + 22, *aempty = bar + 24, *tfull = bar + 26, *tempty = bar + 30;
+    uint64_t *full = bar, *empty = bar + 8, *cfull = bar + 16, *cempty = cfull + kCtxBufs;
+    uint64_t *afull = cempty + kCtxBufs, *aempty = afull + 2, *tfull = aempty + 2, *tempty = tfull + kTileRing;
     uint32_t *s_tmem = reinterpret_cast<uint32_t *>(base + Cfg::kOffMisc);
     volatile int *s_abort = reinterpret_cast<volatile int *>(base + Cfg::kOffMisc + 4);
 
