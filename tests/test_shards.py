@@ -142,3 +142,32 @@ def test_gpu_shards_reproduce_unsharded_rows(how):
     merged = shards.merge_rows(coords.shape[0], parts)
     torch.cuda.synchronize()
     assert torch.equal(merged, full)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_bench_batch_split_renumbers_samples_and_matches_unsharded(world):
+    """bench.py's strong-scaling split: rank r takes the samples b % world == r, renumbered
+    b // world on a grid of its own samples; every row lands on exactly one rank and each rank's
+    float64 oracle conv equals the unsharded one on its rows."""
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    from sparseconv import synthetic
+    w = synthetic.cube(seed=3, batch=4, res=16, p=0.1)
+    full_nbr = oracle.neighbor_map(w.coords, w.shape, w.kernel_size, w.dilation)
+    full = oracle.conv_gather_f64(w.feats.double().numpy(), full_nbr, w.weight.double().numpy())
+    seen = np.zeros(w.num_voxels, dtype=np.int64)
+    for r in range(world):
+        loc = bench._batch_local(w, r, world)
+        assert loc.shape[0] == len(range(r, 4, world))
+        assert loc.coords[:, 0].max() < loc.shape[0]
+        rows = np.nonzero(w.coords[:, 0] % world == r)[0]
+        seen[rows] += 1
+        np.testing.assert_array_equal(loc.coords[:, 1:], w.coords[rows, 1:])
+        nbr = oracle.neighbor_map(loc.coords, loc.shape, loc.kernel_size, loc.dilation)
+        out = oracle.conv_gather_f64(loc.feats.double().numpy(), nbr, loc.weight.double().numpy())
+        np.testing.assert_array_equal(out, full[rows])
+    assert (seen == 1).all()
