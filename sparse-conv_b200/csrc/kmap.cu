@@ -1285,8 +1285,18 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     if (radix) hist = nullptr;
 
     stage_mark(SPCONV_STAGE_MEMSET, 0, stream);
-    if (cudaMemsetAsync(workspace, 0, (size_t)L.total, stream) != cudaSuccess)
+    if (L.bitmap_words && M >= kSortMinVoxels) {
+        // Everything after the table first (the bitmap is the bulk of it), the table last, so
+        // the table's lines are the most recently written when the insert's atomics reach them
+        // (indoor: insert 71 -> 60 us for +3 us of memset; below 2^19 voxels the second memset
+        // costs more than it saves).
+        const int64_t tail = L.table + align256(L.cap * 8) + (key64 ? align256(L.cap * 4) : 0);
+        if (cudaMemsetAsync(ws + tail, 0, (size_t)(L.total - tail), stream) != cudaSuccess ||
+            cudaMemsetAsync(ws, 0, (size_t)tail, stream) != cudaSuccess)
+            return check_launch("workspace memset");
+    } else if (cudaMemsetAsync(workspace, 0, (size_t)L.total, stream) != cudaSuccess) {
         return check_launch("workspace memset");
+    }
     stage_mark(SPCONV_STAGE_MEMSET, 1, stream);
     const int64_t gi = (M + 255) / 256;
     const int ins_grid = (int)(gi < 65535LL * 32 ? gi : 65535LL * 32);
