@@ -121,10 +121,11 @@ def _traffic_per_launch(key: str):
     return None
 
 
-def _launches_per_step(M: int, V: int) -> int:
+def _launches_per_step(M: int, V: int, cells: int) -> int:
     """Kernels one forward launches: insert, map, order (one bucket scatter, or three per 8-bit
-    radix pass for maps of >= 2^19 voxels of <= 27-offset kernels), conv."""
-    if M >= (1 << 19) and V <= 27:
+    radix pass for maps of <= 27-offset kernels of >= 2^19 voxels, or of > 2^17 voxels filling
+    at most 0.3 % of the grid), conv."""
+    if V <= 27 and (M >= (1 << 19) or ((1 << 17) < M <= 0.003 * cells)):
         drop = max(V - 21, 0)
         passes = (4 + V - 1 - drop + 7) // 8
         return 2 + 3 * passes + 1
@@ -544,7 +545,8 @@ def main():
                     "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()), "steps": KE,
                     "pipelined": f"{NS} CUDA streams: step i+1's H2D overlaps step i's op and D2H",
                     "serial_value": e2e_serial},
-            "gpu_launches": _launches_per_step(w.num_voxels, int(np.prod(w.kernel_size))) * K,
+            "gpu_launches": _launches_per_step(w.num_voxels, int(np.prod(w.kernel_size)),
+                                               int(w.shape[0]) * int(np.prod(w.shape[2:]))) * K,
             "clocks": clk,
         }
         if train is not None:

@@ -36,7 +36,7 @@ constexpr int kOrderBuckets = 4096;    // 16 popcount classes x 256 mask-hash bu
 constexpr int kMapThreads = 128;      // one thread per voxel
 constexpr int kOrderThreads = 256;      // kOrderBuckets / kOrderThreads must be a multiple of 4
 constexpr int kOrderPerThread = 2;     // voxels per thread in order_kernel
-// Radix-sort order (kernels of at most kSortMaxV offsets, at least kSortMinVoxels voxels):
+// Radix-sort order (kernels of at most kSortMaxV offsets; see radix_order for the sizes):
 // tiles of kSortTile voxels, 8-bit digits, keys of at most 31 bits.
 constexpr int kSortThreads = 512;
 constexpr int kSortWarpItems = 128;                                  // 4 rounds of 32 per warp
@@ -44,6 +44,13 @@ constexpr int kSortTile = (kSortThreads / 32) * kSortWarpItems;      // 2048 (40
 constexpr int kSortMaxPasses = 4;
 constexpr int kSortMaxV = 27;
 constexpr int64_t kSortMinVoxels = 1 << 19;
+// Sparse grids (surfaces) gain from the radix order at smaller sizes too: measured per-rank
+// sizes of the benchmark's batch split, map build + conv, B200: indoor 2 samples (500k voxels,
+// 0.19 % of the grid) 469 -> 386 us, 1 sample (250k) 272 -> 256 us; dense random occupancy
+// loses (cube 168k at 2 %: 80 -> 104 us; wide3 4 samples, 335k at 0.5 %: 147 -> 175 us), and so
+// do clustered LiDAR points at 0.11 % (2 samples, 207k: 156 -> 176 us), the cost of this rule.
+constexpr int64_t kSortSparseMinVoxels = 1 << 17;     // exclusive
+constexpr long double kSortSparseDensity = 0.003L;
 constexpr int kMaxKernelVolume = 1024;
 
 static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
@@ -106,7 +113,16 @@ static bool volume_fits_32(int batch, int W, int H, int D) {
     return vol < 4294967296.0L;
 }
 
-static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
+// Whether a map of M voxels on an N x W x H x D grid is ordered by the radix sort (when its
+// kernel has at most kSortMaxV offsets): from 2^19 voxels, or above 2^17 voxels on grids they
+// fill to at most 0.3 %. (Measured: see kSortSparseMinVoxels.)
+static bool radix_order(int64_t M, int batch, int W, int H, int D) {
+    if (M >= kSortMinVoxels) return true;
+    const long double vol = (long double)batch * W * H * D;
+    return M > kSortSparseMinVoxels && (long double)M <= kSortSparseDensity * vol;
+}
+
+static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words, bool sort) {
     WsLayout L;
     L.cap = capacity_for(M);
     L.key64 = key64;
@@ -118,7 +134,7 @@ static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words) {
     L.hist = off; off += align256(kOrderBuckets * 4);
     L.cursor = off; off += align256(kOrderBuckets * 4);
     L.flags = off; off += 256;          // per-call flags, cleared with the rest (word 0: duplicate seen)
-    if (M >= kSortMinVoxels) {
+    if (sort) {
         // Sort keys and values (4 x M words) reuse the table, dead once the map is built:
         // its capacity is at least 2M slots of 8 bytes.
         L.sort_tiles = (int)((M + kSortTile - 1) / kSortTile);
@@ -1233,16 +1249,16 @@ extern "C" int spconv_mask_words(int kernel_volume) {
 
 extern "C" int64_t spconv_neighbor_map_workspace_bytes(int64_t num_coords, int batch, int W, int H, int D) {
     if (num_coords < 0) return -1;
-    return ws_layout(num_coords, !volume_fits_32(batch, W, H, D), bitmap_words_for(batch, W, H, D)).total;
+    return ws_layout(num_coords, !volume_fits_32(batch, W, H, D), bitmap_words_for(batch, W, H, D),
+                     radix_order(num_coords, batch, W, H, D)).total;
 }
 
-extern "C" int spconv_build_submanifold_neighbor_map(
-    const int32_t *coords, int64_t M,
-    int batch, int W, int H, int D,
-    int Kw, int Kh, int Kd, int Dw, int Dh, int Dd,
-    void *workspace, int64_t workspace_bytes,
-    int32_t *neighbor_map, uint32_t *masks, int32_t *order,
-    int32_t *status, void *stream_ptr) {
+namespace spconv {
+// The map build; allow_radix = false keeps the bucket order at every size (the fixed scratch of
+// the allocation-free entry point has no room for the radix sort's counts).
+static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, int D, int Kw, int Kh, int Kd,
+                     int Dw, int Dh, int Dd, void *workspace, int64_t workspace_bytes, int32_t *neighbor_map,
+                     uint32_t *masks, int32_t *order, int32_t *status, void *stream_ptr, bool allow_radix) {
     SPCONV_REQUIRE(M >= 0, SPCONV_ERR_ARG, "num_coords must be >= 0 (got %lld)", (long long)M);
     SPCONV_REQUIRE(M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld exceeds 2^31-1 rows", (long long)M);
     SPCONV_REQUIRE(batch > 0 && W > 0 && H > 0 && D > 0, SPCONV_ERR_ARG,
@@ -1263,8 +1279,9 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     SPCONV_REQUIRE(((uintptr_t)workspace & 255u) == 0, SPCONV_ERR_ARG, "workspace must be 256-byte aligned");
     const bool key64 = !volume_fits_32(batch, W, H, D);
     // The occupancy bitmap is used when the workspace has room for it.
-    WsLayout L = ws_layout(M, key64, bitmap_words_for(batch, W, H, D));
-    if (L.bitmap_words && workspace_bytes < L.total) L = ws_layout(M, key64, 0);
+    const bool sort = allow_radix && radix_order(M, batch, W, H, D);
+    WsLayout L = ws_layout(M, key64, bitmap_words_for(batch, W, H, D), sort);
+    if (L.bitmap_words && workspace_bytes < L.total) L = ws_layout(M, key64, 0, sort);
     SPCONV_REQUIRE(workspace_bytes >= L.total, SPCONV_ERR_ARG,
                    "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)L.total);
     cudaStream_t stream = (cudaStream_t)stream_ptr;
@@ -1280,7 +1297,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     for (int64_t c = L.cap / kGroup; c > 1; c >>= 1) --shift;   // 32 - log2(groups)
     const int MW = spconv_mask_words(V);
     // Stable radix-sort order for kernels of <= kSortMaxV offsets when the workspace has room
-    // (M >= kSortMinVoxels); the map kernels then skip the bucket histogram.
+    // (radix_order); the map kernels then skip the bucket histogram.
     const bool radix = L.sort_tiles > 0 && V <= kSortMaxV;
     if (radix) hist = nullptr;
 
@@ -1387,6 +1404,18 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     stage_mark(SPCONV_STAGE_ORDER, 1, stream);
     return SPCONV_OK;
 }
+}  // namespace spconv
+
+extern "C" int spconv_build_submanifold_neighbor_map(
+    const int32_t *coords, int64_t M,
+    int batch, int W, int H, int D,
+    int Kw, int Kh, int Kd, int Dw, int Dh, int Dd,
+    void *workspace, int64_t workspace_bytes,
+    int32_t *neighbor_map, uint32_t *masks, int32_t *order,
+    int32_t *status, void *stream_ptr) {
+    return build_map(coords, M, batch, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, workspace, workspace_bytes,
+                     neighbor_map, masks, order, status, stream_ptr, true);
+}
 
 // ---------------------------------------------------------------------------------------
 // Allocation-free variant: the workspace is a fixed file-scope device array.
@@ -1405,14 +1434,11 @@ constexpr int64_t noalloc_capacity() { return capacity_for((int64_t)SPCONV_NOALL
 constexpr int64_t align256c(int64_t x) { return (x + 255) & ~int64_t(255); }
 // The largest layout ws_layout gives for at most SPCONV_NOALLOC_MAX_COORDS voxels: 64-bit keys
 // (table + row array), no bitmap, histogram, cursors and the per-call flags. The radix-sort counts are absent
-// because such inputs stay below kSortMinVoxels (checked below); a 32-bit-key layout is smaller,
+// because that entry point keeps the bucket order at every size it accepts; a 32-bit-key layout is smaller,
 // and its bitmap is dropped when it does not fit.
 constexpr int64_t kNoAllocScratchBytes =
     align256c(noalloc_capacity() * 8) + align256c(noalloc_capacity() * 4) +
     2 * align256c(kOrderBuckets * 4) + 256 /* per-call flags */ + 256;
-static_assert((int64_t)SPCONV_NOALLOC_MAX_COORDS < kSortMinVoxels,
-              "the no-alloc scratch has no room for the radix-sort counts: raise "
-              "kNoAllocScratchBytes to cover ws_layout's sort_counts before raising the limit");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -1459,9 +1485,9 @@ extern "C" int spconv_build_submanifold_neighbor_map_noalloc(
     if (M > 0) {
         if (int rc = noalloc_scratch(&scratch)) return rc;
     }
-    return spconv_build_submanifold_neighbor_map(
+    return build_map(
         coords, M, batch, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, scratch, kNoAllocScratchBytes,
-        neighbor_map, masks, order, status, stream);
+        neighbor_map, masks, order, status, stream, false);
 }
 
 // ---------------------------------------------------------------------------------------
