@@ -28,10 +28,11 @@ batches would run them); ``e2e.serial_value`` is the same with every step on one
 ``--impl reference`` times the reference's CPU path on this host instead: the oracle's C
 restatement of the reference map builder (OpenMP, all cores, every voxel) plus the reference's
 EXPLICIT_GEMM forward restated on CPU torch in fp32 (all threads) over a row sample of the map
-(at most 2^27 im2col elements), scaled to the whole workload; rank 0 only. The same line
-carries ``reference_gpu``: the reference's own GPU forward (its CUDA map builder compiled from
-its sources + its Triton implicit GEMM, through its public ``sparse_submanifold_conv3d``) timed
-on cuda:0 by ``oracle/ref_gpu.py`` in a separate process.
+(at most 2^27 im2col elements), scaled to the whole workload; rank 0 only. That line and, at
+N=1, this library's own line carry ``reference_gpu``: the reference's own GPU forward (its CUDA
+map builder compiled from its sources + its Triton implicit GEMM, through its public
+``sparse_submanifold_conv3d``) timed on cuda:0 by ``oracle/ref_gpu.py`` in a separate process
+(``--no-reference-gpu`` leaves it out of this library's line).
 """
 from __future__ import annotations
 
@@ -275,6 +276,8 @@ def main():
                     help="N>1: split the workload's batch over the ranks (strong scaling) or give "
                          "every rank its own full batch (weak scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="N=1: skip timing the reference's own GPU forward beside this line")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--e2e-streams", type=int, default=2, help="CUDA streams the end-to-end steps rotate over")
     ap.add_argument("--no-backward", action="store_true", help="skip the training-step (forward + backward) figure")
@@ -553,6 +556,9 @@ def main():
             line["training_step"] = train
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w)
+        if world == 1 and not args.no_reference_gpu:
+            # the reference's own GPU forward on the same workload and device (separate process)
+            line["reference_gpu"] = _reference_gpu(args.workload, 5, 3)
         print(json.dumps(line), flush=True)
     if pg is not None:
         torch.distributed.barrier()

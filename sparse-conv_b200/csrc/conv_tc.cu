@@ -52,6 +52,10 @@ constexpr int kActMax = 32;         // active offsets per context buffer
 #ifndef SPCONV_TC_CTX_BUFS_1CTA
 #define SPCONV_TC_CTX_BUFS_1CTA 5
 #endif
+// Stages (A + B tile) up to this many bytes run two CTAs per SM, larger ones one.
+#ifndef SPCONV_TC_2CTA_MAX_STAGE
+#define SPCONV_TC_2CTA_MAX_STAGE (12 * 1024)
+#endif
 #ifndef SPCONV_TC_CTX_BUFS_2CTA
 #define SPCONV_TC_CTX_BUFS_2CTA 4
 #endif
@@ -89,7 +93,8 @@ struct TcCfg {
     // Whole-row staging pays where the gatherers are fast relative to the index loads (rows of
     // at most 64 bytes); wider rows keep the smaller per-offset buffers and one more stage.
     static constexpr bool kRows = KC <= 32;
-    static constexpr int kCtxBufs = kABytes + kBBytes <= 12 * 1024 ? SPCONV_TC_CTX_BUFS_2CTA : SPCONV_TC_CTX_BUFS_1CTA;
+    static constexpr bool kTwoCtas = kABytes + kBBytes <= SPCONV_TC_2CTA_MAX_STAGE;   // two CTAs per SM
+    static constexpr int kCtxBufs = kTwoCtas ? SPCONV_TC_CTX_BUFS_2CTA : SPCONV_TC_CTX_BUFS_1CTA;
     // mbarriers: full[8] empty[8] cfull[ctx] cempty[ctx] afull[2] aempty[2] tfull[ring] tempty[ring]
     static constexpr int kNumBars = 16 + 2 * kCtxBufs + 4 + 2 * kTileRing;
     static constexpr int kBufWords = kTileM * (kRows ? kRowWindow : kNPitch);   // one context buffer
@@ -99,8 +104,8 @@ struct TcCfg {
     static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kActMax * 4 + kCtxBufs * 16 +
                                        kTileRing * kTileM * 4 + kTileRing * 4 + kMaxStages * 4 + kNumBars * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
-    static constexpr int kBudget = kStageBytes <= 12 * 1024 ? 110 * 1024 : 219 * 1024;
-    static constexpr int kMinBlocks = kStageBytes <= 12 * 1024 ? 2 : 1;   // registers for two CTAs
+    static constexpr int kBudget = kTwoCtas ? 110 * 1024 : 219 * 1024;
+    static constexpr int kMinBlocks = kTwoCtas ? 2 : 1;   // registers for two CTAs
     static constexpr int kStagesFit = (kBudget - kFixedBytes - 1024) / kStageBytes;
     static constexpr int kStages = kStagesFit > kMaxStages ? kMaxStages : (kStagesFit < 3 ? 3 : kStagesFit);
     static constexpr int kDepth = kStages - 1;             // cp.async groups in flight per gatherer

@@ -55,6 +55,16 @@ constexpr int kMaxKernelVolume = 1024;
 
 static int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+// Sorted-input path (section 2c'): at most this many (b, x, y) columns (64 MB of ranges).
+constexpr int64_t kSortedMaxCols = 1ll << 23;
+// Columns of the grid when the sorted-input path can serve it (32-bit keys), else 0.
+static int64_t sorted_cols(int batch, int W, int H, int D) {
+    const long double vol = (long double)batch * W * H * D;
+    const long double cols = (long double)batch * W * H;
+    if (vol >= 4294967296.0L || cols > (long double)kSortedMaxCols) return 0;
+    return (int64_t)cols;
+}
+
 // Table capacity for M voxels: the next power of two >= 4M (load <= 0.25) while the table
 // stays within 64 MB (L2-resident next to the streams it serves), else >= 2M (load <= 0.5).
 // Slots are probed in aligned groups of kGroup = 4 (one 32-byte sector per probe).
@@ -77,6 +87,8 @@ struct WsLayout {
     int64_t table = 0, vals = 0, bitmap = 0, hist = 0, cursor = 0, flags = 0, total = 0;
     int sort_tiles = 0;            // > 0: room for the radix-sort order (keys alias the table)
     int64_t sort_counts = 0;       // [kSortMaxPasses][256][sort_tiles] + [kSortMaxPasses][256] totals
+    int64_t cols = 0;              // > 0: room for the sorted-input path (column ranges + keys)
+    int64_t colrange = 0, keys = 0;
 };
 
 // Grids of at most 2^30 cells (a 128 MB bitmap, cleared with the table) get an occupancy
@@ -122,7 +134,9 @@ static bool radix_order(int64_t M, int batch, int W, int H, int D) {
     return M > kSortSparseMinVoxels && (long double)M <= kSortSparseDensity * vol;
 }
 
-static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words, bool sort) {
+// `cols` > 0 adds the sorted-input path's regions: [cols] int2 column ranges (cleared with the
+// histogram and flags) and [M] uint32 flat keys.
+static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words, bool sort, int64_t cols = 0) {
     WsLayout L;
     L.cap = capacity_for(M);
     L.key64 = key64;
@@ -140,6 +154,11 @@ static WsLayout ws_layout(int64_t M, bool key64, int64_t bitmap_words, bool sort
         L.sort_tiles = (int)((M + kSortTile - 1) / kSortTile);
         L.sort_counts = off;
         off += align256((int64_t)kSortMaxPasses * 256 * (L.sort_tiles + 1) * 4);
+    }
+    if (cols > 0 && !key64) {
+        L.cols = cols;
+        L.colrange = off; off += align256(cols * 8);
+        L.keys = off; off += align256(M * 4);
     }
     L.total = off;
     return L;
@@ -257,8 +276,9 @@ template <bool KEY64>
 __global__ void __launch_bounds__(256)
 insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, int D,
               unsigned long long *table, uint32_t *vals, uint32_t *bitmap, uint64_t gmask,
-              uint32_t shift, int32_t *status, int32_t *dup_flag) {
+              uint32_t shift, int32_t *status, int32_t *dup_flag, const int32_t *unsorted) {
     grid_launch_dependents();                                   // the map kernel's setup overlaps this
+    if (unsorted && *unsorted == 0) return;                     // sorted input: the column path builds the map
     const int lane = threadIdx.x & 31;
     // Whole warps iterate together (the bitmap update below shuffles across the warp).
     for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < M;
@@ -584,7 +604,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
               uint32_t *__restrict__ masks, uint32_t *hist,
-              int32_t *status, const int32_t *dup_flag) {
+              int32_t *status, const int32_t *dup_flag, const int32_t *unsorted) {
     constexpr int V = 27;
     __shared__ uint32_t s_hist[kOrderBuckets];
     __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
@@ -611,6 +631,7 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     const uint32_t zbits = (in_z[0] ? 1u : 0u) | 2u | (in_z[2] ? 4u : 0u);
 
     grid_dependency_wait();                                     // the insert's table and bitmap
+    if (unsorted && *unsorted == 0) return;                     // sorted input: the column path builds the map
     grid_launch_dependents();
     // Phase 1: candidate offsets.
     uint32_t cand = 0;
@@ -735,6 +756,206 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     __syncthreads();
     {
         // The block's rows form one contiguous range of the map (16-byte aligned: i0 % 256 == 0).
+        int32_t *out = nbr + i0 * (int64_t)V;
+        const int total = nvox * V;
+        const int n4 = total >> 2;
+        const int4 *src = reinterpret_cast<const int4 *>(s_stage);
+        int4 *dst = reinterpret_cast<int4 *>(out);
+        for (int e = tid; e < n4; e += kMapK3Threads) dst[e] = src[e];
+        for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
+    }
+    if (hist) block_hist_flush(s_hist, hist);
+}
+
+// ---------------------------------------------------------------------------------------
+// 2c'. Sorted-input path for 3x3x3 kernels (grids of < 2^32 cells and at most
+//      kSortedMaxCols (b, x, y) columns). Coordinates as SparseConvTensor.from_dense and
+//      voxelisers produce them - strictly increasing in (b, x, y, z) - need no hash table:
+//      the rows of a column (b, x, y) are one contiguous range of the input, sorted by z, so
+//      a neighbour is found by a binary search of the flat keys inside its column's range.
+//      sorted_prep_kernel writes the flat keys, each occupied column's [first, last + 1) row
+//      range (the array is cleared per call, so empty columns read as (0, 0)) and a per-call
+//      word that is set when any row is out of range or not above its predecessor (unsorted
+//      or duplicate input). The hash kernels above return at once when that word is clear,
+//      map_sorted_k3 when it is set, so one of the two paths builds the map, with no host
+//      synchronisation. For unique coordinates every neighbour is one row, so both paths
+//      give the same map, masks and order keys bit for bit.
+// ---------------------------------------------------------------------------------------
+constexpr int kPrepThreads = 256;
+
+__global__ void __launch_bounds__(kPrepThreads)
+sorted_prep_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, int D,
+                   uint32_t *__restrict__ keys, int2 *__restrict__ colrange, int32_t *unsorted) {
+    const int64_t i = (int64_t)blockIdx.x * kPrepThreads + threadIdx.x;
+    auto in_range = [&](const int4 &c) {
+        return c.x >= 0 && c.x < N && c.y >= 0 && c.y < W && c.z >= 0 && c.z < H && c.w >= 0 && c.w < D;
+    };
+    auto column = [&](const int4 &c) { return ((int64_t)c.x * W + c.y) * H + c.z; };
+    bool bad = false;
+    if (i < M) {
+        const int4 c = __ldg(coords + i);
+        if (!in_range(c)) {
+            bad = true;
+        } else {
+            const int64_t col = column(c);
+            const int64_t key = col * D + c.w;
+            keys[i] = (uint32_t)key;
+            bool first = true, last = true;
+            if (i > 0) {
+                const int4 p = __ldg(coords + i - 1);
+                if (in_range(p)) {               // an out-of-range row flags itself
+                    const int64_t pcol = column(p);
+                    if (pcol * D + p.w >= key) bad = true;
+                    first = pcol != col;
+                }
+            }
+            if (i + 1 < M) {
+                const int4 n = __ldg(coords + i + 1);
+                if (in_range(n)) last = column(n) != col;
+            }
+            if (first) colrange[col].x = (int32_t)i;
+            if (last) colrange[col].y = (int32_t)(i + 1);
+        }
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) *unsorted = 1;
+}
+
+// Clears the hash path's table and bitmap (`n16` 16-byte words from `p`), unless the input
+// took the sorted path. Highest addresses first, so the table (at the start) is the most
+// recently written when the insert's atomics reach it.
+__global__ void __launch_bounds__(256)
+clear_unless_sorted_kernel(uint4 *__restrict__ p, int64_t n16, const int32_t *unsorted) {
+    if (*unsorted == 0) return;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n16; j += (int64_t)gridDim.x * blockDim.x)
+        p[n16 - 1 - j] = z;
+}
+
+// One thread per voxel, 256 voxels per block, for strictly increasing coordinates. The nine
+// (dx, dy) columns' ranges are loaded together; the nine lower-bound searches (for the lowest
+// in-range z target of each column) advance in lockstep, so their key loads are in flight
+// together; then each column's next rows (at most 2*Dd + 1, all inside the column) are
+// matched against z - Dd, z and z + Dd. With Dd = 1 the voxel's own z - 1 / z + 1 neighbours
+// can only be rows i - 1 / i + 1. Rows are staged in shared memory and written out
+// coalesced; masks and order histogram as in map_kernel_k3.
+template <bool DD1>
+__global__ void __launch_bounds__(kMapK3Threads, 4)
+map_sorted_k3(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys,
+              const int2 *__restrict__ colrange, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
+              int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist,
+              const int32_t *unsorted) {
+    constexpr int V = 27;
+    __shared__ uint32_t s_hist[kOrderBuckets];
+    __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
+    if (*unsorted != 0) return;                                 // the hash path builds this map
+
+    const int tid = threadIdx.x;
+    const int64_t i0 = (int64_t)blockIdx.x * kMapK3Threads;
+    const int nvox = (M - i0) < (int64_t)kMapK3Threads ? (int)(M - i0) : kMapK3Threads;
+    for (int j = tid; j < kOrderBuckets; j += kMapK3Threads) s_hist[j] = 0u;
+    {
+        int4 *st4 = reinterpret_cast<int4 *>(s_stage);
+        for (int j = tid; j < kMapK3Threads * V / 4; j += kMapK3Threads) st4[j] = make_int4(-1, -1, -1, -1);
+    }
+    const bool valid = tid < nvox;
+    const int64_t i = i0 + tid;
+    int4 c = make_int4(0, 0, 0, 0);
+    if (valid) c = __ldg(coords + i);
+    const int64_t col_c = ((int64_t)c.x * W + c.y) * H + c.z;
+    const int64_t key_c = col_c * D + c.w;
+    const bool in_x[3] = {c.y - Dw >= 0, true, c.y + Dw < W};
+    const bool in_y[3] = {c.z - Dh >= 0, true, c.z + Dh < H};
+    const bool lo_z = c.w - Dd >= 0, hi_z = c.w + Dd < D;
+    const int zlo = lo_z ? Dd : 0;                              // lowest target: z - zlo
+
+    int lo[9], len[9], end[9];
+    uint32_t target[9];
+#pragma unroll
+    for (int q = 0; q < 9; ++q) {
+        const int dx = q / 3 - 1, dy = q % 3 - 1;
+        lo[q] = 0;
+        len[q] = 0;
+        end[q] = 0;
+        const int64_t cq = col_c + (int64_t)dx * Dw * H + (int64_t)dy * Dh;
+        target[q] = (uint32_t)(cq * D + c.w - zlo);
+        if (valid && in_x[dx + 1] && in_y[dy + 1] && !(DD1 && q == 4)) {
+            const int2 r = __ldg(colrange + cq);
+            lo[q] = r.x;
+            end[q] = r.y;
+            len[q] = r.y > r.x ? r.y - r.x : 0;
+        }
+    }
+    // Lockstep lower bounds: lo[q] = first row of the column whose key >= target[q].
+    for (;;) {
+        bool more = false;
+#pragma unroll
+        for (int q = 0; q < 9; ++q) {
+            if (len[q] > 0) {
+                const int half = len[q] >> 1;
+                if (__ldg(keys + lo[q] + half) < target[q]) {
+                    lo[q] += half + 1;
+                    len[q] -= half + 1;
+                } else {
+                    len[q] = half;
+                }
+                more |= len[q] > 0;
+            }
+        }
+        if (!more) break;
+    }
+
+    __syncthreads();                                            // hist zeroed, stage pre-filled
+    uint32_t bits = valid ? (1u << (V / 2)) : 0u;
+    if (valid) {
+        s_stage[tid * V + V / 2] = (int32_t)i;
+        if (DD1) {                                              // own column: rows i - 1, i + 1
+            if (lo_z && i > 0 && __ldg(keys + i - 1) == (uint32_t)(key_c - 1)) {
+                s_stage[tid * V + V / 2 - 1] = (int32_t)(i - 1);
+                bits |= 1u << (V / 2 - 1);
+            }
+            if (hi_z && i + 1 < M && __ldg(keys + i + 1) == (uint32_t)(key_c + 1)) {
+                s_stage[tid * V + V / 2 + 1] = (int32_t)(i + 1);
+                bits |= 1u << (V / 2 + 1);
+            }
+        }
+        const int walk = DD1 ? 3 : 2 * Dd + 1;
+#pragma unroll
+        for (int q = 0; q < 9; ++q) {
+            if (DD1 && q == 4) continue;
+            // keys of this column from its lowest target on: dz = key - target - zlo + ... ;
+            // rel = key - target is the z distance above the lowest target (0 .. 2*Dd).
+#pragma unroll 3
+            for (int s = 0; s < walk; ++s) {
+                const int j = lo[q] + s;
+                if (j >= end[q]) break;
+                const uint32_t rel = __ldg(keys + j) - target[q];
+                if (rel > (uint32_t)(zlo + Dd)) break;
+                // rel = zlo - Dd + (dz_index) * Dd for the targets z - Dd, z, z + Dd
+                int e = -1;
+                if (lo_z && rel == 0u) e = 0;
+                else if (rel == (uint32_t)zlo) e = 1;
+                else if (hi_z && rel == (uint32_t)(zlo + Dd)) e = 2;
+                if (e >= 0) {
+                    const int v = q * 3 + e;
+                    if (v != V / 2) {
+                        s_stage[tid * V + v] = j;
+                        bits |= 1u << v;
+                    }
+                }
+            }
+        }
+        masks[i] = bits;
+    }
+    {
+        const uint32_t pc = __popc(bits);
+        const uint32_t h = fmix32(0x9e3779b9u ^ bits);
+        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t active = __ballot_sync(0xffffffffu, valid);
+        if (valid && hist) aggregated_inc(s_hist, k, active);
+    }
+    __syncthreads();
+    {
         int32_t *out = nbr + i0 * (int64_t)V;
         const int total = nvox * V;
         const int n4 = total >> 2;
@@ -1250,7 +1471,7 @@ extern "C" int spconv_mask_words(int kernel_volume) {
 extern "C" int64_t spconv_neighbor_map_workspace_bytes(int64_t num_coords, int batch, int W, int H, int D) {
     if (num_coords < 0) return -1;
     return ws_layout(num_coords, !volume_fits_32(batch, W, H, D), bitmap_words_for(batch, W, H, D),
-                     radix_order(num_coords, batch, W, H, D)).total;
+                     radix_order(num_coords, batch, W, H, D), sorted_cols(batch, W, H, D)).total;
 }
 
 namespace spconv {
@@ -1258,7 +1479,8 @@ namespace spconv {
 // the allocation-free entry point has no room for the radix sort's counts).
 static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, int D, int Kw, int Kh, int Kd,
                      int Dw, int Dh, int Dd, void *workspace, int64_t workspace_bytes, int32_t *neighbor_map,
-                     uint32_t *masks, int32_t *order, int32_t *status, void *stream_ptr, bool allow_radix) {
+                     uint32_t *masks, int32_t *order, int32_t *status, void *stream_ptr, bool allow_radix,
+                     bool allow_sorted) {
     SPCONV_REQUIRE(M >= 0, SPCONV_ERR_ARG, "num_coords must be >= 0 (got %lld)", (long long)M);
     SPCONV_REQUIRE(M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld exceeds 2^31-1 rows", (long long)M);
     SPCONV_REQUIRE(batch > 0 && W > 0 && H > 0 && D > 0, SPCONV_ERR_ARG,
@@ -1280,7 +1502,11 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     const bool key64 = !volume_fits_32(batch, W, H, D);
     // The occupancy bitmap is used when the workspace has room for it.
     const bool sort = allow_radix && radix_order(M, batch, W, H, D);
-    WsLayout L = ws_layout(M, key64, bitmap_words_for(batch, W, H, D), sort);
+    // The sorted-input path serves 3x3x3 kernels (section 2c'); its regions are used when the
+    // workspace has room for them, the occupancy bitmap when it has room for that.
+    const int64_t cols = (allow_sorted && Kw == 3 && Kh == 3 && Kd == 3) ? sorted_cols(batch, W, H, D) : 0;
+    WsLayout L = ws_layout(M, key64, bitmap_words_for(batch, W, H, D), sort, cols);
+    if (L.cols && workspace_bytes < L.total) L = ws_layout(M, key64, bitmap_words_for(batch, W, H, D), sort);
     if (L.bitmap_words && workspace_bytes < L.total) L = ws_layout(M, key64, 0, sort);
     SPCONV_REQUIRE(workspace_bytes >= L.total, SPCONV_ERR_ARG,
                    "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)L.total);
@@ -1301,8 +1527,23 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     const bool radix = L.sort_tiles > 0 && V <= kSortMaxV;
     if (radix) hist = nullptr;
 
+    int32_t *unsorted = L.cols ? dup_flag + 1 : nullptr;       // per-call word: the hash path runs
+    uint32_t *keys = L.cols ? (uint32_t *)(ws + L.keys) : nullptr;
+
     stage_mark(SPCONV_STAGE_MEMSET, 0, stream);
-    if (L.bitmap_words && M >= kSortMinVoxels) {
+    if (L.cols) {
+        // Histogram, cursors, flags, sort counts and column ranges are cleared for every input;
+        // the table and bitmap only when the input takes the hash path.
+        if (cudaMemsetAsync(ws + L.hist, 0, (size_t)(L.keys - L.hist), stream) != cudaSuccess)
+            return check_launch("workspace memset");
+        const int64_t pb = (M + kPrepThreads - 1) / kPrepThreads;
+        sorted_prep_kernel<<<(unsigned)pb, kPrepThreads, 0, stream>>>(
+            (const int4 *)coords, M, batch, W, H, D, keys, (int2 *)(ws + L.colrange), unsorted);
+        if (int rc = check_launch("sorted_prep_kernel")) return rc;
+        const int64_t n16 = L.hist / 16;                        // table (+ rows) + bitmap
+        clear_unless_sorted_kernel<<<148 * 8, 256, 0, stream>>>((uint4 *)ws, n16, unsorted);
+        if (int rc = check_launch("clear_unless_sorted_kernel")) return rc;
+    } else if (L.bitmap_words && M >= kSortMinVoxels) {
         // Everything after the table first (the bitmap is the bulk of it), the table last, so
         // the table's lines are the most recently written when the insert's atomics reach them
         // (indoor: insert 71 -> 60 us for +3 us of memset; below 2^19 voxels the second memset
@@ -1319,9 +1560,9 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     const int ins_grid = (int)(gi < 65535LL * 32 ? gi : 65535LL * 32);
     stage_mark(SPCONV_STAGE_INSERT, 0, stream);
     if (key64)
-        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag);
+        insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag, unsorted);
     else
-        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag);
+        insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag, unsorted);
     if (int rc = check_launch("insert_kernel")) return rc;
     stage_mark(SPCONV_STAGE_INSERT, 1, stream);
 
@@ -1332,7 +1573,14 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
         launch_pdl(k3_fn, dim3(grid), dim3(kMapK3Threads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, (const unsigned long long *)table,
                    (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
-                   status, (const int32_t *)dup_flag);
+                   status, (const int32_t *)dup_flag, (const int32_t *)unsorted);
+        if (L.cols) {
+            if (int rc = check_launch("map_kernel_k3")) return rc;
+            auto sk = Dd == 1 ? map_sorted_k3<true> : map_sorted_k3<false>;
+            sk<<<grid, kMapK3Threads, 0, stream>>>((const int4 *)coords, (const uint32_t *)keys,
+                                                  (const int2 *)(ws + L.colrange), M, W, H, D, Dw, Dh, Dd,
+                                                  neighbor_map, masks, hist, (const int32_t *)unsorted);
+        }
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
         const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
@@ -1414,7 +1662,7 @@ extern "C" int spconv_build_submanifold_neighbor_map(
     int32_t *neighbor_map, uint32_t *masks, int32_t *order,
     int32_t *status, void *stream_ptr) {
     return build_map(coords, M, batch, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, workspace, workspace_bytes,
-                     neighbor_map, masks, order, status, stream_ptr, true);
+                     neighbor_map, masks, order, status, stream_ptr, true, true);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1487,7 +1735,7 @@ extern "C" int spconv_build_submanifold_neighbor_map_noalloc(
     }
     return build_map(
         coords, M, batch, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, scratch, kNoAllocScratchBytes,
-        neighbor_map, masks, order, status, stream, false);
+        neighbor_map, masks, order, status, stream, false, false);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1511,7 +1759,9 @@ static int64_t coords4_bytes(int64_t M) { return align256(M * 16); }
 
 extern "C" int64_t spconv_neighbor_map_2d_workspace_bytes(int64_t num_coords, int batch, int W, int H) {
     if (num_coords < 0) return -1;
-    const int64_t b3 = spconv_neighbor_map_workspace_bytes(num_coords, batch, W, H, 1);
+    // the 3-D layout with D = 1 and no sorted-input regions (the 2-D kernel is not 3x3x3)
+    const int64_t b3 = ws_layout(num_coords, !volume_fits_32(batch, W, H, 1), bitmap_words_for(batch, W, H, 1),
+                                 radix_order(num_coords, batch, W, H, 1)).total;
     return b3 < 0 ? -1 : b3 + coords4_bytes(num_coords);
 }
 

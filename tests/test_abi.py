@@ -65,12 +65,17 @@ def test_workspace_bytes(lib):
     # <= 2^30 cells: table + a one-bit-per-cell occupancy bitmap
     small_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 4, 128, 128, 128)
     assert small_grid >= 8 * cap + 4 * 128 ** 3 // 8
-    # 2^30 < cells < 2^32: table only
+    # 2^30 < cells < 2^32: table only, plus the sorted-input path's column ranges (8 bytes per
+    # (b, x, y) column, at most 2^23 columns) and flat keys (4 bytes per voxel)
     mid_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 16, 512, 512, 512)
-    assert 8 * cap <= mid_grid < 8 * cap + 64 * 1024
+    sorted_regions = 16 * 512 * 512 * 8 + (1000 * 4 + 255) // 256 * 256
+    assert 8 * cap <= mid_grid - sorted_regions < 8 * cap + 64 * 1024
+    # more than 2^23 columns: no sorted-input regions
+    many_cols = lib.spconv_neighbor_map_workspace_bytes(1000, 64, 2048, 128, 128)
+    assert 8 * cap <= many_cols < 8 * cap + 64 * 1024
     # >= 2^32 cells: 64-bit keys add a row array
     big_grid = lib.spconv_neighbor_map_workspace_bytes(1000, 2, 2048, 2048, 1024)
-    assert big_grid >= 12 * cap and big_grid > mid_grid
+    assert big_grid >= 12 * cap and big_grid > mid_grid - sorted_regions
     assert lib.spconv_neighbor_map_workspace_bytes(-1, 1, 1, 1, 1) == -1
 
 

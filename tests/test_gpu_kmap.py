@@ -179,9 +179,13 @@ def test_hash_only_path_matches_bitmap_path(name):
     lib = _native.load_library()
     c = torch.from_numpy(coords).cuda()
     M, V = coords.shape[0], ks[0] * ks[1] * ks[2]
-    with_bitmap = _native.workspace_bytes(M, N, W, H, D)
-    bitmap_bytes = ((((N * W * H * D) + 31) // 32) * 4 + 255) // 256 * 256
-    ws = torch.empty((with_bitmap - bitmap_bytes,), dtype=torch.uint8, device="cuda")
+    full = _native.workspace_bytes(M, N, W, H, D)
+    a256 = lambda x: (x + 255) // 256 * 256
+    bitmap_bytes = a256((((N * W * H * D) + 31) // 32) * 4)
+    # 3x3x3 kernels on grids of < 2^32 cells and <= 2^23 columns also get the sorted-input
+    # path's column ranges and keys; leave them out too, so only the hash table remains.
+    sorted_bytes = a256(N * W * H * 8) + a256(M * 4) if N * W * H * D < 2 ** 32 and N * W * H <= 2 ** 23 else 0
+    ws = torch.empty((full - bitmap_bytes - sorted_bytes,), dtype=torch.uint8, device="cuda")
     nbr = torch.empty((M, V), dtype=torch.int32, device="cuda")
     masks = torch.empty((M, (V + 31) // 32), dtype=torch.int32, device="cuda")
     order = torch.empty((M,), dtype=torch.int32, device="cuda")
@@ -205,3 +209,63 @@ def test_radix_order_large_maps(ks, dil):
     assert coords.shape[0] >= RADIX_MIN_VOXELS
     nbr, masks, order = gpu_map(coords, (B, 1, R, R, R), ks, dil)
     check_masks_and_order(nbr, masks, order)
+
+
+def _edge_coords(seed, B, W, H, D, p):
+    """Random voxels plus every cell on the z = 0 and z = D - 1 faces of some columns, so that
+    flat keys of neighbouring columns are adjacent (z = D - 1 of one column, z = 0 of the
+    next): a z +- d neighbour must never be taken from the next or previous column."""
+    rng = np.random.default_rng(seed)
+    occ = rng.random((B, W, H, D)) < p
+    occ[:, :, :, 0] |= rng.random((B, W, H)) < 0.5
+    occ[:, :, :, D - 1] |= rng.random((B, W, H)) < 0.5
+    occ[:, 0, :, :] |= rng.random((B, H, D)) < 0.3
+    occ[:, W - 1, :, :] |= rng.random((B, H, D)) < 0.3
+    return np.ascontiguousarray(np.argwhere(occ).astype(np.int32))
+
+
+@pytest.mark.parametrize("dil", [(1, 1, 1), (2, 2, 2), (1, 2, 3), (3, 1, 2)])
+def test_sorted_path_column_edges(dil):
+    """Sorted 3x3x3 input takes the column path (binary searches inside each (b, x, y)
+    column's row range): grid faces and adjacent-column keys, several dilations."""
+    B, W, H, D = 2, 9, 7, 6
+    coords = _edge_coords(21, B, W, H, D, 0.15)
+    shape = (B, 1, W, H, D)
+    nbr, masks, order = gpu_map(coords, shape, (3, 3, 3), dil)
+    np.testing.assert_array_equal(nbr, oracle.neighbor_map(coords, shape, (3, 3, 3), dil))
+    check_masks_and_order(nbr, masks, order)
+
+
+@pytest.mark.parametrize("swap", ["adjacent", "far", "equal"])
+def test_nearly_sorted_input_takes_the_hash_path(swap):
+    """One out-of-order pair (or one repeated row) in otherwise sorted input: the device-side
+    sortedness test sends the build to the hash path, whose map must still be the oracle's."""
+    coords, shape, ks, dil = gpu_cases.small_cases()["dense3"]
+    c = coords.copy()
+    M = c.shape[0]
+    if swap == "adjacent":
+        c[[M // 2, M // 2 + 1]] = c[[M // 2 + 1, M // 2]]
+    elif swap == "far":
+        c[[5, M - 5]] = c[[M - 5, 5]]
+    else:
+        c[M // 3] = c[M // 3 - 1]
+    _native.reset_status()
+    nbr, masks, order = gpu_map(c, shape, ks, dil)
+    np.testing.assert_array_equal(nbr, oracle.neighbor_map(c, shape, ks, dil))
+    _native.reset_status()
+
+
+def test_sorted_then_unsorted_reuse_one_workspace():
+    """Alternating sorted and shuffled inputs through one workspace: each call clears what its
+    path reads (column ranges every call, table and bitmap on the hash path)."""
+    coords, shape, ks, dil = gpu_cases.small_cases()["rand3"]
+    N, _C, W, H, D = shape
+    perm = np.random.default_rng(5).permutation(coords.shape[0])
+    shuffled = np.ascontiguousarray(coords[perm])
+    M = coords.shape[0]
+    ws = torch.empty((_native.workspace_bytes(M, N, W, H, D),), dtype=torch.uint8, device="cuda")
+    for c in (coords, shuffled, coords, shuffled):
+        t = torch.from_numpy(c).cuda()
+        nbr, _m, _o = _native.build_neighbor_map(t, N, W, H, D, ks, dil, workspace=ws)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(nbr.cpu().numpy().view(np.uint32), oracle.neighbor_map(c, shape, ks, dil))
