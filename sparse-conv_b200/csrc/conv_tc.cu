@@ -39,7 +39,13 @@
 namespace spconv {
 
 constexpr int kTileM = 128;
-constexpr int kChunk = 16;          // active offsets per context
+#ifndef SPCONV_TC_CHUNK
+#define SPCONV_TC_CHUNK 16
+#endif
+#ifndef SPCONV_TC_2CTA_BUDGET_KB
+#define SPCONV_TC_2CTA_BUDGET_KB 110
+#endif
+constexpr int kChunk = SPCONV_TC_CHUNK;   // active offsets per context (a power of two <= 16)
 constexpr int kNPitch = kChunk + 1; // words per row in a context buffer (conflict-free both ways)
 constexpr int kRowWindow = 32;      // words per staged index row: a 128-byte aligned window
 constexpr int kRowsMaxV = 28;       // V for which a voxel's whole index row fits one window
@@ -52,9 +58,13 @@ constexpr int kActMax = 32;         // active offsets per context buffer
 #ifndef SPCONV_TC_CTX_BUFS_1CTA
 #define SPCONV_TC_CTX_BUFS_1CTA 5
 #endif
-// Stages (A + B tile) up to this many bytes run two CTAs per SM, larger ones one.
+// Stages (A + B tile) up to this many bytes run two CTAs per SM, larger ones one. Random
+// 128-byte row gathers by cp.async reach about twice the rate with two CTAs per SM as with one
+// at the same warp count (B200, indoor index stream: 4.7-5.0 TB/s with one CTA of 4, 8 or 16
+// warps, 8.4-8.9 TB/s with two), so C = 64 stages (24 KB: 3 stages, 4 index contexts) run two
+// CTAs: indoor conv 793 -> 605 us.
 #ifndef SPCONV_TC_2CTA_MAX_STAGE
-#define SPCONV_TC_2CTA_MAX_STAGE (12 * 1024)
+#define SPCONV_TC_2CTA_MAX_STAGE (24 * 1024)
 #endif
 #ifndef SPCONV_TC_CTX_BUFS_2CTA
 #define SPCONV_TC_CTX_BUFS_2CTA 4
@@ -104,7 +114,7 @@ struct TcCfg {
     static constexpr int kFixedBytes = kNBytes + kSchedBytes + kCtxBufs * kActMax * 4 + kCtxBufs * 16 +
                                        kTileRing * kTileM * 4 + kTileRing * 4 + kMaxStages * 4 + kNumBars * 8 + 16;
     // Small stages: about 110 KB per CTA (two CTAs per SM); large: one CTA per SM.
-    static constexpr int kBudget = kTwoCtas ? 110 * 1024 : 219 * 1024;
+    static constexpr int kBudget = kTwoCtas ? SPCONV_TC_2CTA_BUDGET_KB * 1024 : 219 * 1024;
     static constexpr int kMinBlocks = kTwoCtas ? 2 : 1;   // registers for two CTAs
     static constexpr int kStagesFit = (kBudget - kFixedBytes - 1024) / kStageBytes;
     static constexpr int kStages = kStagesFit > kMaxStages ? kMaxStages : (kStagesFit < 3 ? 3 : kStagesFit);

@@ -599,15 +599,13 @@ constexpr int kMapK3Threads = 256;
 constexpr int kK3Batch = 4;
 
 template <bool BITMAP>
-__global__ void __launch_bounds__(kMapK3Threads, 4)
-map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
+__device__ __forceinline__ void
+k3_hash_block(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
               uint32_t *__restrict__ masks, uint32_t *hist,
-              int32_t *status, const int32_t *dup_flag, const int32_t *unsorted) {
+              int32_t *status, const int32_t *dup_flag, uint32_t *s_hist, int32_t *s_stage) {
     constexpr int V = 27;
-    __shared__ uint32_t s_hist[kOrderBuckets];
-    __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
 
     const int tid = threadIdx.x;
     const int64_t i0 = (int64_t)blockIdx.x * kMapK3Threads;
@@ -630,8 +628,6 @@ map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     const bool in_z[3] = {c.w - Dd >= 0, true, c.w + Dd < D};
     const uint32_t zbits = (in_z[0] ? 1u : 0u) | 2u | (in_z[2] ? 4u : 0u);
 
-    grid_dependency_wait();                                     // the insert's table and bitmap
-    if (unsorted && *unsorted == 0) return;                     // sorted input: the column path builds the map
     grid_launch_dependents();
     // Phase 1: candidate offsets.
     uint32_t cand = 0;
@@ -834,21 +830,17 @@ clear_unless_sorted_kernel(uint4 *__restrict__ p, int64_t n16, const int32_t *un
 // One thread per voxel, 256 voxels per block, for strictly increasing coordinates. The nine
 // (dx, dy) columns' ranges are loaded together; the nine lower-bound searches (for the lowest
 // in-range z target of each column) advance in lockstep, so their key loads are in flight
-// together; then each column's next rows (at most 2*Dd + 1, all inside the column) are
-// matched against z - Dd, z and z + Dd. With Dd = 1 the voxel's own z - 1 / z + 1 neighbours
-// can only be rows i - 1 / i + 1. Rows are staged in shared memory and written out
-// coalesced; masks and order histogram as in map_kernel_k3.
+// together; then the next 2*Dd + 1 rows of every column (those inside it) are loaded together
+// and matched against z - Dd, z and z + Dd. With Dd = 1 the voxel's own z - 1 / z + 1
+// neighbours can only be rows i - 1 / i + 1. Rows are staged in shared memory and written out
+// coalesced; masks and order histogram as in k3_hash_block.
 template <bool DD1>
-__global__ void __launch_bounds__(kMapK3Threads, 4)
-map_sorted_k3(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys,
-              const int2 *__restrict__ colrange, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
-              int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist,
-              const int32_t *unsorted) {
+__device__ __forceinline__ void
+k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys,
+                const int2 *__restrict__ colrange, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
+                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist,
+                uint32_t *s_hist, int32_t *s_stage) {
     constexpr int V = 27;
-    __shared__ uint32_t s_hist[kOrderBuckets];
-    __shared__ __align__(16) int32_t s_stage[kMapK3Threads * V];   // read back as int4
-    if (*unsorted != 0) return;                                 // the hash path builds this map
-
     const int tid = threadIdx.x;
     const int64_t i0 = (int64_t)blockIdx.x * kMapK3Threads;
     const int nvox = (M - i0) < (int64_t)kMapK3Threads ? (int)(M - i0) : kMapK3Threads;
@@ -857,6 +849,7 @@ map_sorted_k3(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys
         int4 *st4 = reinterpret_cast<int4 *>(s_stage);
         for (int j = tid; j < kMapK3Threads * V / 4; j += kMapK3Threads) st4[j] = make_int4(-1, -1, -1, -1);
     }
+    grid_launch_dependents();
     const bool valid = tid < nvox;
     const int64_t i = i0 + tid;
     int4 c = make_int4(0, 0, 0, 0);
@@ -908,41 +901,61 @@ map_sorted_k3(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys
     uint32_t bits = valid ? (1u << (V / 2)) : 0u;
     if (valid) {
         s_stage[tid * V + V / 2] = (int32_t)i;
-        if (DD1) {                                              // own column: rows i - 1, i + 1
-            if (lo_z && i > 0 && __ldg(keys + i - 1) == (uint32_t)(key_c - 1)) {
+        // rel = key - target: the z distance above the lowest target; the targets z - Dd, z and
+        // z + Dd sit at rel = 0 (when z - Dd is in range), zlo and zlo + Dd (when in range).
+        auto match = [&](int q, int j, uint32_t key) {
+            const uint32_t rel = key - target[q];
+            int e = -1;
+            if (lo_z && rel == 0u) e = 0;
+            else if (rel == (uint32_t)zlo) e = 1;
+            else if (hi_z && rel == (uint32_t)(zlo + Dd)) e = 2;
+            const int v = q * 3 + e;
+            if (e >= 0 && v != V / 2) {
+                s_stage[tid * V + v] = j;
+                bits |= 1u << v;
+            }
+        };
+        if (DD1) {
+            // every column's next three rows (those inside the column) and rows i - 1, i + 1
+            const bool has_m = lo_z && i > 0, has_p = hi_z && i + 1 < M;
+            const uint32_t km = has_m ? __ldg(keys + i - 1) : 0u;
+            const uint32_t kp = has_p ? __ldg(keys + i + 1) : 0u;
+            // The next three rows of columns 0-3, then of columns 5-8, loaded together (twelve
+            // loads in flight, registers for no more); rows outside the column read as
+            // target - 1 (rel = 2^32 - 1 matches no target).
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t kk[4][3];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int q = half * 5 + u;
+#pragma unroll
+                    for (int s = 0; s < 3; ++s) {
+                        const int j = lo[q] + s;
+                        kk[u][s] = j < end[q] ? __ldg(keys + j) : target[q] - 1u;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int s = 0; s < 3; ++s) match(half * 5 + u, lo[half * 5 + u] + s, kk[u][s]);
+            }
+            if (has_m && km == (uint32_t)(key_c - 1)) {
                 s_stage[tid * V + V / 2 - 1] = (int32_t)(i - 1);
                 bits |= 1u << (V / 2 - 1);
             }
-            if (hi_z && i + 1 < M && __ldg(keys + i + 1) == (uint32_t)(key_c + 1)) {
+            if (has_p && kp == (uint32_t)(key_c + 1)) {
                 s_stage[tid * V + V / 2 + 1] = (int32_t)(i + 1);
                 bits |= 1u << (V / 2 + 1);
             }
-        }
-        const int walk = DD1 ? 3 : 2 * Dd + 1;
+        } else {
+            const int walk = 2 * Dd + 1;
 #pragma unroll
-        for (int q = 0; q < 9; ++q) {
-            if (DD1 && q == 4) continue;
-            // keys of this column from its lowest target on: dz = key - target - zlo + ... ;
-            // rel = key - target is the z distance above the lowest target (0 .. 2*Dd).
-#pragma unroll 3
-            for (int s = 0; s < walk; ++s) {
-                const int j = lo[q] + s;
-                if (j >= end[q]) break;
-                const uint32_t rel = __ldg(keys + j) - target[q];
-                if (rel > (uint32_t)(zlo + Dd)) break;
-                // rel = zlo - Dd + (dz_index) * Dd for the targets z - Dd, z, z + Dd
-                int e = -1;
-                if (lo_z && rel == 0u) e = 0;
-                else if (rel == (uint32_t)zlo) e = 1;
-                else if (hi_z && rel == (uint32_t)(zlo + Dd)) e = 2;
-                if (e >= 0) {
-                    const int v = q * 3 + e;
-                    if (v != V / 2) {
-                        s_stage[tid * V + v] = j;
-                        bits |= 1u << v;
-                    }
+            for (int q = 0; q < 9; ++q)
+                for (int s = 0; s < walk; ++s) {
+                    const int j = lo[q] + s;
+                    if (j < end[q]) match(q, j, __ldg(keys + j));
                 }
-            }
         }
         masks[i] = bits;
     }
@@ -965,6 +978,26 @@ map_sorted_k3(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys
         for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
     }
     if (hist) block_hist_flush(s_hist, hist);
+}
+
+// The 3x3x3 map kernel: the column path when this call's input is strictly increasing (the
+// prep kernel left `unsorted` clear), else the hash path; the word is read once per block
+// after the previous kernels are complete, so every block takes the same path.
+template <bool BITMAP, bool DD1>
+__global__ void __launch_bounds__(kMapK3Threads, 4)
+map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
+              const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
+              int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
+              uint32_t *__restrict__ masks, uint32_t *hist, int32_t *status, const int32_t *dup_flag,
+              const uint32_t *__restrict__ keys, const int2 *__restrict__ colrange, const int32_t *unsorted) {
+    __shared__ uint32_t s_hist[kOrderBuckets];
+    __shared__ __align__(16) int32_t s_stage[kMapK3Threads * 27];   // read back as int4
+    grid_dependency_wait();                                     // the insert's table / the prep's keys
+    if (unsorted && *unsorted == 0)
+        k3_sorted_block<DD1>(coords, keys, colrange, M, W, H, D, Dw, Dh, Dd, nbr, masks, hist, s_hist, s_stage);
+    else
+        k3_hash_block<BITMAP>(coords, M, W, H, D, Dw, Dh, Dd, table, bitmap, bm_words, gmask, shift, nbr, masks,
+                              hist, status, dup_flag, s_hist, s_stage);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1557,7 +1590,10 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     }
     stage_mark(SPCONV_STAGE_MEMSET, 1, stream);
     const int64_t gi = (M + 255) / 256;
-    const int ins_grid = (int)(gi < 65535LL * 32 ? gi : 65535LL * 32);
+    // Where the input may take the sorted path the insert usually returns at once: a grid of
+    // 16 blocks per SM (grid-stride) keeps that cheap; otherwise one thread per voxel.
+    const int64_t gcap = L.cols ? 148LL * 16 : 65535LL * 32;
+    const int ins_grid = (int)(gi < gcap ? gi : gcap);
     stage_mark(SPCONV_STAGE_INSERT, 0, stream);
     if (key64)
         insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag, unsorted);
@@ -1567,20 +1603,15 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     stage_mark(SPCONV_STAGE_INSERT, 1, stream);
 
     if (!key64 && Kw == 3 && Kh == 3 && Kd == 3) {
-        auto k3_fn = bitmap ? map_kernel_k3<true> : map_kernel_k3<false>;
+        auto k3_fn = bitmap ? (Dd == 1 ? map_kernel_k3<true, true> : map_kernel_k3<true, false>)
+                            : (Dd == 1 ? map_kernel_k3<false, true> : map_kernel_k3<false, false>);
         const int grid = (int)((M + kMapK3Threads - 1) / kMapK3Threads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         launch_pdl(k3_fn, dim3(grid), dim3(kMapK3Threads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, (const unsigned long long *)table,
                    (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
-                   status, (const int32_t *)dup_flag, (const int32_t *)unsorted);
-        if (L.cols) {
-            if (int rc = check_launch("map_kernel_k3")) return rc;
-            auto sk = Dd == 1 ? map_sorted_k3<true> : map_sorted_k3<false>;
-            sk<<<grid, kMapK3Threads, 0, stream>>>((const int4 *)coords, (const uint32_t *)keys,
-                                                  (const int2 *)(ws + L.colrange), M, W, H, D, Dw, Dh, Dd,
-                                                  neighbor_map, masks, hist, (const int32_t *)unsorted);
-        }
+                   status, (const int32_t *)dup_flag, (const uint32_t *)keys,
+                   (const int2 *)(L.cols ? ws + L.colrange : nullptr), (const int32_t *)unsorted);
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
         const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
