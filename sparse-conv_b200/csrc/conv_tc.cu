@@ -39,6 +39,18 @@
 namespace spconv {
 
 constexpr int kTileM = 128;
+// Index contexts the scheduler keeps loading before it publishes the oldest (see the
+// scheduler): 1 publishes each context when the next one has been issued.
+#ifndef SPCONV_TC_SCHED_PEND
+#define SPCONV_TC_SCHED_PEND 1
+#endif
+// Channels per K step (the A row width: 64 bf16 = one 128-byte swizzle row).
+#ifndef SPCONV_TC_MAX_KC
+#define SPCONV_TC_MAX_KC 64
+#endif
+#ifndef SPCONV_TC_ROWS_MAX_KC
+#define SPCONV_TC_ROWS_MAX_KC 32
+#endif
 #ifndef SPCONV_TC_CHUNK
 #define SPCONV_TC_CHUNK 16
 #endif
@@ -93,7 +105,7 @@ constexpr int kTileEnd = -2;        // tile-ring info of the epilogue's end mark
 
 template <int CI, int CO>
 struct TcCfg {
-    static constexpr int KC = CI > 64 ? 64 : CI;          // channels per K step
+    static constexpr int KC = CI > SPCONV_TC_MAX_KC ? SPCONV_TC_MAX_KC : CI;   // channels per K step
     static constexpr int NKC = CI / KC;
     static constexpr int kRowBytes = KC * 2;               // = swizzle width (32, 64, 128)
     static constexpr int kLanesPerRow = kRowBytes / 16;    // = rows per lane in a gather warp
@@ -102,7 +114,7 @@ struct TcCfg {
     static constexpr int kStageBytes = kABytes + kBBytes;
     // Whole-row staging pays where the gatherers are fast relative to the index loads (rows of
     // at most 64 bytes); wider rows keep the smaller per-offset buffers and one more stage.
-    static constexpr bool kRows = KC <= 32;
+    static constexpr bool kRows = CI <= SPCONV_TC_ROWS_MAX_KC;
     static constexpr bool kTwoCtas = kABytes + kBBytes <= SPCONV_TC_2CTA_MAX_STAGE;   // two CTAs per SM
     static constexpr int kCtxBufs = kTwoCtas ? SPCONV_TC_CTX_BUFS_2CTA : SPCONV_TC_CTX_BUFS_1CTA;
     // mbarriers: full[8] empty[8] cfull[ctx] cempty[ctx] afull[2] aempty[2] tfull[ring] tempty[ring]
@@ -281,15 +293,30 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
         load_masks(rA, mA);
         load_masks(rB, mB);
         int g = 0;                           // contexts handed out
-        int pend = -1;                       // context buffer whose index loads are in flight
+        // Context buffers whose index loads are in flight, oldest first. After each new context
+        // the oldest is published once at most kPend groups remain outstanding, so up to
+        // kPend + 1 contexts load at once. kPend < kCtxBufs: a buffer the scheduler waits to
+        // reuse was published at least one context earlier, and (kTileRing = 4 > kPend) the
+        // tile whose ring slot it waits for has every context published.
+        constexpr int kPend = SPCONV_TC_SCHED_PEND < kCtxBufs ? SPCONV_TC_SCHED_PEND : kCtxBufs - 1;
+        static_assert(kPend >= 1 && kPend < kTileRing, "scheduler look-ahead");
+        // Contexts gp .. g-1 are issued and not yet published (buffer = context % kCtxBufs).
+        int gp = 0;
         bool ok = true;
-        auto publish_pending = [&](bool all) {
-            if (pend < 0) return;
-            if (all) cp_async_wait<0>();
-            else cp_async_wait<1>();
+        auto publish_oldest = [&]() {
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&cfull[pend]));
-            pend = -1;
+            if (lane == 0) mbar_arrive(smem_u32(&cfull[gp % kCtxBufs]));
+            ++gp;
+        };
+        auto push_pending = [&]() {          // context g's cp.async group is committed
+            if (g + 1 - gp > kPend) {
+                cp_async_wait<kPend>();
+                publish_oldest();
+            }
+        };
+        auto publish_all = [&]() {           // after the last context (g = contexts issued)
+            cp_async_wait<0>();
+            while (gp < g) publish_oldest();
         };
         int kt = 0;                          // tiles (non-empty items) handed to the MMA and epilogue
         for (int k = 0; k < nt && ok; ++k) {
@@ -393,8 +420,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 cp_async_commit();
                 left = 0;
                 if (lane == 0) s_cinfo[cb] = make_int4(kt, cnt, kCtxFirst | kCtxLast | kCtxRows, 0);
-                publish_pending(false);      // the previous tile's rows have landed
-                pend = cb;
+                push_pending();
                 ++g;
             }
             while (left > 0) {
@@ -434,8 +460,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
                 left -= cnt;
                 if (lane == 0) s_cinfo[cb] = make_int4(kt, cnt, (first ? kCtxFirst : 0) | (left == 0 ? kCtxLast : 0), 0);
                 first = false;
-                publish_pending(false);      // the previous context's loads have landed
-                pend = cb;
+                push_pending();
                 ++g;
             }
             if (!ok) break;
@@ -452,7 +477,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T *__restrict__
             load_masks(rB, mB);
             load_rows(k + 3, rC);
         }
-        publish_pending(true);
+        publish_all();
         if (SPLIT && ok) {                   // end marker for the epilogue (item count varies)
             const int t = kt % kTileRing;
             if (kt < kTileRing || wait(&tempty[t], (uint32_t)(((kt / kTileRing) - 1) & 1))) {

@@ -6,7 +6,9 @@
 // (neighbor_map.cu:132-177) that writes only the found entries.
 //
 // Here:
-//   1. one cudaMemsetAsync clears the workspace (table, bitmap, histogram, cursors);
+//   1. one cudaMemsetAsync clears the workspace (table, bitmap, histogram, cursors); for
+//      3x3x3 kernels the prep kernel of the sorted-input path (section 2c') runs first and the
+//      table and bitmap are cleared by a kernel only when the input takes the hash path;
 //   2. insert_kernel: one thread per voxel, a coalesced int4 load, a CAS into the first free
 //      slot of its 32-byte group of a power-of-two table of packed 64-bit slots
 //      ((key << 32) | row, stored complemented so that all-zero means empty), and the
@@ -278,6 +280,7 @@ insert_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int H, i
               unsigned long long *table, uint32_t *vals, uint32_t *bitmap, uint64_t gmask,
               uint32_t shift, int32_t *status, int32_t *dup_flag, const int32_t *unsorted) {
     grid_launch_dependents();                                   // the map kernel's setup overlaps this
+    grid_dependency_wait();                                     // the cleared table (launched with PDL)
     if (unsorted && *unsorted == 0) return;                     // sorted input: the column path builds the map
     const int lane = threadIdx.x & 31;
     // Whole warps iterate together (the bitmap update below shuffles across the warp).
@@ -821,6 +824,8 @@ sorted_prep_kernel(const int4 *__restrict__ coords, int64_t M, int N, int W, int
 // recently written when the insert's atomics reach it.
 __global__ void __launch_bounds__(256)
 clear_unless_sorted_kernel(uint4 *__restrict__ p, int64_t n16, const int32_t *unsorted) {
+    grid_dependency_wait();                                     // the prep kernel's word
+    grid_launch_dependents();
     if (*unsorted == 0) return;
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
     for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n16; j += (int64_t)gridDim.x * blockDim.x)
@@ -1574,7 +1579,8 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
             (const int4 *)coords, M, batch, W, H, D, keys, (int2 *)(ws + L.colrange), unsorted);
         if (int rc = check_launch("sorted_prep_kernel")) return rc;
         const int64_t n16 = L.hist / 16;                        // table (+ rows) + bitmap
-        clear_unless_sorted_kernel<<<148 * 8, 256, 0, stream>>>((uint4 *)ws, n16, unsorted);
+        launch_pdl(clear_unless_sorted_kernel, dim3(148 * 8), dim3(256), 0, stream, (uint4 *)ws, n16,
+                   (const int32_t *)unsorted);
         if (int rc = check_launch("clear_unless_sorted_kernel")) return rc;
     } else if (L.bitmap_words && M >= kSortMinVoxels) {
         // Everything after the table first (the bitmap is the bulk of it), the table last, so
@@ -1597,6 +1603,9 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     stage_mark(SPCONV_STAGE_INSERT, 0, stream);
     if (key64)
         insert_kernel<true><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag, unsorted);
+    else if (L.cols)     // after the clear kernel: its launch overlaps that kernel's tail
+        launch_pdl(insert_kernel<false>, dim3(ins_grid), dim3(256), 0, stream, (const int4 *)coords, M, batch, W, H, D,
+                   table, vals, bitmap, gmask, shift, status, dup_flag, (const int32_t *)unsorted);
     else
         insert_kernel<false><<<ins_grid, 256, 0, stream>>>((const int4 *)coords, M, batch, W, H, D, table, vals, bitmap, gmask, shift, status, dup_flag, unsorted);
     if (int rc = check_launch("insert_kernel")) return rc;
