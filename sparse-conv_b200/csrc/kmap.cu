@@ -881,6 +881,9 @@ k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ ke
             lo[q] = r.x;
             end[q] = r.y;
             len[q] = r.y > r.x ? r.y - r.x : 0;
+            // A column no longer than the walk below is walked whole from its first row: no
+            // search (most surface columns hold one to three voxels).
+            if (len[q] <= (DD1 ? 3 : 2 * Dd + 1)) len[q] = 0;
         }
     }
     // Lockstep lower bounds: lo[q] = first row of the column whose key >= target[q].
@@ -927,7 +930,7 @@ k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ ke
             const uint32_t kp = has_p ? __ldg(keys + i + 1) : 0u;
             // The next three rows of columns 0-3, then of columns 5-8, loaded together (twelve
             // loads in flight, registers for no more); rows outside the column read as
-            // target - 1 (rel = 2^32 - 1 matches no target).
+            // target + 3 (e >= 3 below: no match).
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t kk[4][3];
@@ -937,13 +940,24 @@ k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ ke
 #pragma unroll
                     for (int s = 0; s < 3; ++s) {
                         const int j = lo[q] + s;
-                        kk[u][s] = j < end[q] ? __ldg(keys + j) : target[q] - 1u;
+                        kk[u][s] = j < end[q] ? __ldg(keys + j) : target[q] + 3u;
                     }
                 }
+                // Dd = 1: the targets z - 1, z, z + 1 are e = rel + 1 - zlo = 0, 1, 2. A row of this
+                // column at z - 1 exists only when z >= 1 and at z + 1 only when z + 1 < D, so no
+                // range test is needed; rows below the lowest target wrap to large e.
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
 #pragma unroll
-                    for (int s = 0; s < 3; ++s) match(half * 5 + u, lo[half * 5 + u] + s, kk[u][s]);
+                    for (int s = 0; s < 3; ++s) {
+                        const int q = half * 5 + u;
+                        const uint32_t e = kk[u][s] - target[q] + 1u - (uint32_t)zlo;
+                        if (e <= 2u) {
+                            const int v = q * 3 + (int)e;
+                            s_stage[tid * V + v] = lo[q] + s;
+                            bits |= 1u << v;
+                        }
+                    }
             }
             if (has_m && km == (uint32_t)(key_c - 1)) {
                 s_stage[tid * V + V / 2 - 1] = (int32_t)(i - 1);
