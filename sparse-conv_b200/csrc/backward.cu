@@ -497,15 +497,46 @@ static int launch_wgrad_mma(const void *feats, const void *gout, const int32_t *
     return check_launch("wgrad_mma_kernel");
 }
 
+#ifndef SPCONV_WGRAD_TC
+#define SPCONV_WGRAD_TC 1
+#endif
+
+// The tcgen05 weight gradient (wgrad_tc.cu) for the shapes it covers: tile unions and the
+// per-group tile lists for its groups of offsets, then the kernel.
+static int launch_wgrad_tc_path(int dtype, const void *feats, const void *gout, const int32_t *nbr,
+                                const uint32_t *masks, const int32_t *order, int64_t M, int V, float *gw,
+                                void *scratch, int32_t *status, cudaStream_t stream) {
+    const int num_tiles = (int)((M + kWgTile - 1) / kWgTile);
+    const int OG = wgrad_tc_group_offsets();
+    const int groups = (V + OG - 1) / OG;
+    const int MW = (V + 31) / 32;
+    uint32_t *uni = (uint32_t *)scratch;
+    int32_t *list = (int32_t *)(uni + (int64_t)num_tiles * MW);
+    int32_t *cnt = list + (int64_t)V * num_tiles;
+    tile_union_kernel<<<num_tiles, kWgTile, 0, stream>>>(MW <= 4 ? masks : nullptr, nbr, order, M, V, MW, uni);
+    if (int rc = check_launch("tile_union_kernel")) return rc;
+    group_tiles_kernel<<<groups, 512, 0, stream>>>(uni, num_tiles, MW, V, OG, list, cnt);
+    if (int rc = check_launch("group_tiles_kernel")) return rc;
+    return launch_wgrad_tc(dtype, feats, gout, nbr, order, uni, list, cnt, M, V, MW, num_tiles, gw, status, stream);
+}
+
 template <typename T>
 static int launch_wgrad_t(const void *feats, const void *gout, const int32_t *nbr, const uint32_t *masks,
                           const int32_t *order, int64_t M, int V, int Ci, int Co, float *gw, float *gb,
-                          void *scratch, cudaStream_t stream) {
+                          void *scratch, int32_t *status, cudaStream_t stream) {
     int rc = SPCONV_OK;
     bool done = false;
     if constexpr (!std::is_same<T, float>::value) {
+        const int dtype = std::is_same<T, __half>::value ? SPCONV_F16 : SPCONV_BF16;
+        if (SPCONV_WGRAD_TC && scratch && wgrad_tc_supported(dtype, Ci, Co, V) && ((uintptr_t)feats & 15u) == 0 &&
+            ((uintptr_t)gout & 15u) == 0) {
+            rc = launch_wgrad_tc_path(dtype, feats, gout, nbr, masks, order, M, V, gw, scratch, status, stream);
+            done = true;
+        }
+    }
+    if constexpr (!std::is_same<T, float>::value) {
         static_assert(kWgMaxGroups >= 1024, "group counts of any kernel volume fit in shared memory");
-        if (((uintptr_t)feats & 15u) == 0 && ((uintptr_t)gout & 15u) == 0 && scratch) {
+        if (!done && ((uintptr_t)feats & 15u) == 0 && ((uintptr_t)gout & 15u) == 0 && scratch) {
 #define SPCONV_WG(CO_, CI_)                                                                  \
             if constexpr (WgCfg<T, CO_, CI_>::kSupported) {                                  \
                 if (!done && Co == CO_ && Ci == CI_) {                                       \
@@ -575,7 +606,6 @@ extern "C" int spconv_submanifold_conv_weight_grad(
     const void *feats, const void *grad_out, int dtype, int64_t M, int Ci, int Co, int V,
     const int32_t *nbr, const uint32_t *masks, const int32_t *order, float *grad_weight, float *grad_bias,
     void *workspace, int64_t workspace_bytes, int32_t *status, void *stream) {
-    (void)status;
     SPCONV_REQUIRE(M >= 0 && M <= 0x7fffffffLL, SPCONV_ERR_ARG, "num_coords %lld out of range", (long long)M);
     SPCONV_REQUIRE(Ci > 0 && Co > 0, SPCONV_ERR_ARG, "channels must be positive (Ci=%d Co=%d)", Ci, Co);
     SPCONV_REQUIRE(V > 0 && V <= 1024, SPCONV_ERR_ARG, "kernel volume %d out of range [1, 1024]", V);
@@ -594,10 +624,10 @@ extern "C" int spconv_submanifold_conv_weight_grad(
     void *scratch = (workspace && workspace_bytes >= wgrad_scratch_bytes(M, V)) ? workspace : nullptr;
     switch (dtype) {
         case SPCONV_F32:
-            return launch_wgrad_t<float>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, s);
+            return launch_wgrad_t<float>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, status, s);
         case SPCONV_F16:
-            return launch_wgrad_t<__half>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, s);
+            return launch_wgrad_t<__half>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, status, s);
         default:
-            return launch_wgrad_t<__nv_bfloat16>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, s);
+            return launch_wgrad_t<__nv_bfloat16>(feats, grad_out, nbr, masks, order, M, V, Ci, Co, grad_weight, grad_bias, scratch, status, s);
     }
 }
