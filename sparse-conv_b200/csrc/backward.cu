@@ -501,25 +501,6 @@ static int launch_wgrad_mma(const void *feats, const void *gout, const int32_t *
 #define SPCONV_WGRAD_TC 1
 #endif
 
-// The tcgen05 weight gradient (wgrad_tc.cu) for the shapes it covers: tile unions and the
-// per-group tile lists for its groups of offsets, then the kernel.
-static int launch_wgrad_tc_path(int dtype, const void *feats, const void *gout, const int32_t *nbr,
-                                const uint32_t *masks, const int32_t *order, int64_t M, int V, float *gw,
-                                void *scratch, int32_t *status, cudaStream_t stream) {
-    const int num_tiles = (int)((M + kWgTile - 1) / kWgTile);
-    const int OG = wgrad_tc_group_offsets();
-    const int groups = (V + OG - 1) / OG;
-    const int MW = (V + 31) / 32;
-    uint32_t *uni = (uint32_t *)scratch;
-    int32_t *list = (int32_t *)(uni + (int64_t)num_tiles * MW);
-    int32_t *cnt = list + (int64_t)V * num_tiles;
-    tile_union_kernel<<<num_tiles, kWgTile, 0, stream>>>(MW <= 4 ? masks : nullptr, nbr, order, M, V, MW, uni);
-    if (int rc = check_launch("tile_union_kernel")) return rc;
-    group_tiles_kernel<<<groups, 512, 0, stream>>>(uni, num_tiles, MW, V, OG, list, cnt);
-    if (int rc = check_launch("group_tiles_kernel")) return rc;
-    return launch_wgrad_tc(dtype, feats, gout, nbr, order, uni, list, cnt, M, V, MW, num_tiles, gw, status, stream);
-}
-
 template <typename T>
 static int launch_wgrad_t(const void *feats, const void *gout, const int32_t *nbr, const uint32_t *masks,
                           const int32_t *order, int64_t M, int V, int Ci, int Co, float *gw, float *gb,
@@ -528,9 +509,10 @@ static int launch_wgrad_t(const void *feats, const void *gout, const int32_t *nb
     bool done = false;
     if constexpr (!std::is_same<T, float>::value) {
         const int dtype = std::is_same<T, __half>::value ? SPCONV_F16 : SPCONV_BF16;
-        if (SPCONV_WGRAD_TC && scratch && wgrad_tc_supported(dtype, Ci, Co, V) && ((uintptr_t)feats & 15u) == 0 &&
+        // the tcgen05 kernel (wgrad_tc.cu) for the shapes it covers; it needs no scratch
+        if (SPCONV_WGRAD_TC && wgrad_tc_supported(dtype, Ci, Co, V) && ((uintptr_t)feats & 15u) == 0 &&
             ((uintptr_t)gout & 15u) == 0) {
-            rc = launch_wgrad_tc_path(dtype, feats, gout, nbr, masks, order, M, V, gw, scratch, status, stream);
+            rc = launch_wgrad_tc(dtype, feats, gout, nbr, order, masks, M, V, gw, status, stream);
             done = true;
         }
     }

@@ -41,13 +41,10 @@ int64_t split_counter_bytes();
 int64_t conv_split_workspace_bytes(int64_t M, int Co);
 int launch_conv_simt(const ConvArgs &a);
 
-// tcgen05 weight gradient (wgrad_tc.cu): 16-bit features with Ci = Co = 64. Offsets in groups
-// of wgrad_tc_group_offsets(); `uni`, `list`, `cnt` are tile_union_kernel's and
-// group_tiles_kernel's outputs for that group size.
+// tcgen05 weight gradient (wgrad_tc.cu): 16-bit features with Ci = Co = 64; `masks` may be null
+// (every offset of a tile is then gathered, missing neighbours as zeros).
 bool wgrad_tc_supported(int dtype, int Ci, int Co, int V);
-int wgrad_tc_group_offsets();
 int launch_wgrad_tc(int dtype, const void *feats, const void *gout, const int32_t *nbr, const int32_t *order,
-                    const uint32_t *uni, const int32_t *list, const int32_t *cnt, int64_t M, int V, int MW,
-                    int num_tiles, float *gw, int32_t *status, cudaStream_t stream);
+                    const uint32_t *masks, int64_t M, int V, float *gw, int32_t *status, cudaStream_t stream);
 
 }  // namespace spconv

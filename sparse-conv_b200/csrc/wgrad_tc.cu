@@ -15,9 +15,9 @@
 // of being gathered.
 //
 // One CTA per SM, 10 warps with fixed roles, synchronised by mbarriers only:
-//   warp 0    scheduler: per work item (tile, group) loads the tile's rows (voxel order), the
-//             tile's offset union (from tile_union_kernel) and, by 4-byte cp.async, the map
-//             entries of the item's active offsets into one of two index contexts;
+//   warp 0    scheduler: per work item (tile, group) loads the tile's rows (voxel order), ORs
+//             their offset masks and, by 4-byte cp.async, loads the map entries of the item's
+//             active offsets into one of two index contexts;
 //   warps 1-4 gatherers: warp g owns rows 32g .. 32g + 31; per item the grad_out rows into
 //             one of two B buffers, then per active pair the feature rows of its active
 //             offsets into an A stage (128-byte swizzled rows, zero fill for missing
@@ -27,8 +27,9 @@
 //   warps 6-9 epilogue: when a CTA's run of items in one group ends, reads each pair's
 //             accumulator (lanes 0-63: offset 2p, lanes 64-127: offset 2p + 1) and adds it to
 //             the fp32 gradient with coalesced atomics.
-// Work items are the (group, tile) pairs with an active offset in the group (group_tiles_kernel),
-// flattened group-major and split into one contiguous range per CTA.
+// Work items are (group, tile) pairs, group-major; CTA c takes items c, c + G, ... (the CTAs walk
+// the tiles side by side, so their gathers share the L2), skipping tiles with no neighbour at
+// any of the group's offsets (the OR of the tile's offset masks).
 // Every wait is bounded (the conv kernels' limit); a timeout raises SPCONV_STATUS_WAIT_TIMEOUT,
 // and the CTA waits (bounded) for its own copies and MMAs before it frees TMEM and exits.
 #include <mutex>
@@ -89,8 +90,7 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t 
 template <typename T>
 __global__ void __launch_bounds__(kWtThreads, 1)
 wgrad_tc_kernel(const T *__restrict__ feats, const T *__restrict__ gout, const int32_t *__restrict__ nbr,
-                const int32_t *__restrict__ order, const uint32_t *__restrict__ uni,
-                const int32_t *__restrict__ list, const int32_t *__restrict__ cnt, int64_t M, int V, int MW,
+                const int32_t *__restrict__ order, const uint32_t *__restrict__ masks, int64_t M, int V, int MW,
                 int num_tiles, int groups, float *__restrict__ gw, int32_t *status, uint64_t wait_ns) {
     constexpr int CI = 64, CO = 64;
     extern __shared__ uint8_t smem_raw[];
@@ -103,7 +103,6 @@ wgrad_tc_kernel(const T *__restrict__ feats, const T *__restrict__ gout, const i
     uint32_t *s_ginfo = reinterpret_cast<uint32_t *>(base + kWtOffGInfo); // B buffer: item flags
     int2 *s_seg = reinterpret_cast<int2 *>(base + kWtOffSeg);             // segment: {group or -1, seen pairs}
     uint32_t *s_pend = reinterpret_cast<uint32_t *>(base + kWtOffPend);   // [gatherer][ring] barrier addresses
-    int32_t *s_gofs = reinterpret_cast<int32_t *>(base + kWtOffCnt);      // [groups + 1] item offsets
     uint64_t *bar = reinterpret_cast<uint64_t *>(base + kWtOffBar);
     uint64_t *full = bar, *empty = bar + kWtStages, *gfull = empty + kWtStages, *gempty = gfull + 2;
     uint64_t *cfull = gempty + 2, *cempty = cfull + kWtCtx, *accfull = cempty + kWtCtx, *accempty = accfull + 1;
@@ -141,30 +140,17 @@ wgrad_tc_kernel(const T *__restrict__ feats, const T *__restrict__ gout, const i
         tmem_alloc(smem_u32(s_tmem), 512);
         tmem_relinquish();
     }
-    // item offsets of the groups (group-major flattening of the per-group tile lists)
-    if (tid == 0) {
-        int acc = 0;
-        for (int g = 0; g < groups; ++g) {
-            s_gofs[g] = acc;
-            acc += __ldg(cnt + g);
-        }
-        s_gofs[groups] = acc;
-    }
     fence_proxy_async_smem();                // the zero blocks, read by the MMAs
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    const int n_items = s_gofs[groups];
+    // Work items k = g * num_tiles + t, taken by CTA c as k = c, c + G, ...: the CTAs walk the
+    // tiles of the voxel order side by side (their gathers share the L2), group after group.
+    const int64_t n_items = (int64_t)groups * num_tiles;
     const int G = gridDim.x;
-    const int k0 = (int)(((int64_t)n_items * blockIdx.x) / G), k1 = (int)(((int64_t)n_items * (blockIdx.x + 1)) / G);
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
         return mbar_wait_or_abort(smem_u32(b), parity, s_abort, wait_ns);
-    };
-    auto group_of = [&](int k) {
-        int g = 0;
-        while (g + 1 < groups && s_gofs[g + 1] <= k) ++g;
-        return g;
     };
 
     if (warp == 0) {
@@ -179,36 +165,49 @@ wgrad_tc_kernel(const T *__restrict__ feats, const T *__restrict__ gout, const i
             if (lane == 0) mbar_arrive(smem_u32(&cfull[pend]));
             pend = -1;
         };
-        int kc = 0;
-        for (int k = k0; k < k1 && ok; ++k, ++kc) {
-            const int g = group_of(k);
-            const int t = __ldg(list + (int64_t)g * num_tiles + (k - s_gofs[g]));
-            const int gn = (k + 1 < k1) ? group_of(k + 1) : -1;
-            const int gp = (k > k0) ? group_of(k - 1) : -1;
-            // the tile's active offsets in this group
+        int kc = 0, g_last = -1;
+        for (int64_t k = blockIdx.x; k < n_items && ok; k += G) {
+            const int g = (int)(k / num_tiles), t = (int)(k - (int64_t)g * num_tiles);
             const int v0 = g * kWtGroupOffsets;
-            uint32_t hm = 0;
-            for (int j = 0; j < kWtGroupOffsets && v0 + j < V; ++j)
-                if ((__ldg(uni + (int64_t)t * MW + ((v0 + j) >> 5)) >> ((v0 + j) & 31)) & 1u) hm |= 1u << j;
-            uint32_t pm = 0;
-            for (int p = 0; p < kWtPairs; ++p)
-                if ((hm >> (2 * p)) & 3u) pm |= 1u << p;
-            const int cb = kc % kWtCtx;
-            if (kc >= kWtCtx && !wait(&cempty[cb], (uint32_t)(((kc / kWtCtx) - 1) & 1))) { ok = false; break; }
-            int32_t *ctx = s_ctx + cb * kWtTile * kWtCols;
             int32_t rows[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int r = lane + 32 * j;
-                const int64_t pos = (int64_t)t * kWtTile + r;
+                const int64_t pos = (int64_t)t * kWtTile + lane + 32 * j;
                 int32_t row = -1;
                 if (pos < M) {
                     row = order ? __ldg(order + pos) : (int32_t)pos;
                     if ((uint32_t)row >= (uint32_t)M) row = -1;
                 }
                 rows[j] = row;
-                ctx[r * kWtCols + kWtGroupOffsets] = row;
             }
+            // the tile's active offsets in this group: its rows' mask bits v0 .. v0 + 15 (all
+            // of the group's offsets when no masks are given)
+            uint32_t hm = 0;
+            const uint32_t valid = (V - v0 >= 32) ? 0xffffu : (((1u << (V - v0)) - 1u) & 0xffffu);
+            if (masks) {
+                const int w0 = v0 >> 5, sh = v0 & 31;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (rows[j] < 0) continue;
+                    const uint32_t *mr = masks + (int64_t)rows[j] * MW;
+                    uint64_t m = __ldg(mr + w0);
+                    if (sh > 16 && w0 + 1 < MW) m |= (uint64_t)__ldg(mr + w0 + 1) << 32;
+                    hm |= (uint32_t)(m >> sh);
+                }
+                hm = __reduce_or_sync(0xffffffffu, hm) & valid;
+            } else {
+                hm = __any_sync(0xffffffffu, rows[0] >= 0) ? valid : 0u;
+            }
+            if (hm == 0u) continue;                               // nothing of this group here
+            uint32_t pm = 0;
+#pragma unroll
+            for (int p = 0; p < kWtPairs; ++p)
+                if ((hm >> (2 * p)) & 3u) pm |= 1u << p;
+            const int cb = kc % kWtCtx;
+            if (kc >= kWtCtx && !wait(&cempty[cb], (uint32_t)(((kc / kWtCtx) - 1) & 1))) { ok = false; break; }
+            int32_t *ctx = s_ctx + cb * kWtTile * kWtCols;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ctx[(lane + 32 * j) * kWtCols + kWtGroupOffsets] = rows[j];
             for (int j = 0; j < kWtGroupOffsets; ++j) {
                 if (!((hm >> j) & 1u)) continue;
                 const int32_t *col = nbr + (v0 + j);
@@ -221,12 +220,18 @@ wgrad_tc_kernel(const T *__restrict__ feats, const T *__restrict__ gout, const i
                 }
             }
             cp_async_commit();
-            if (lane == 0)
-                s_cinfo[cb] = make_int4(k, g, (int)(pm | (hm << 8)),
-                                        (gp != g ? (int)kWtSegFirst : 0) | (gn != g ? (int)kWtSegLast : 0));
+            if (lane == 0) {
+                s_cinfo[cb] = make_int4((int)(k & 0x7fffffff), g, (int)(pm | (hm << 8)), g != g_last ? (int)kWtSegFirst : 0);
+                // the previous context closes its segment when the group changes here
+                if (pend >= 0 && g != g_last) s_cinfo[pend].w |= (int)kWtSegLast;
+            }
+            g_last = g;
             publish(false);
             pend = cb;
+            ++kc;
         }
+        if (lane == 0 && pend >= 0) s_cinfo[pend].w |= (int)kWtSegLast;   // the last context closes its segment
+        __syncwarp();
         publish(true);
         if (ok) {                            // end marker
             const int cb = kc % kWtCtx;
@@ -441,12 +446,11 @@ bool wgrad_tc_supported(int dtype, int Ci, int Co, int V) {
            (V + kWtGroupOffsets - 1) / kWtGroupOffsets <= kWtMaxGroups;
 }
 
-int wgrad_tc_group_offsets() { return kWtGroupOffsets; }
-
 int launch_wgrad_tc(int dtype, const void *feats, const void *gout, const int32_t *nbr, const int32_t *order,
-                    const uint32_t *uni, const int32_t *list, const int32_t *cnt, int64_t M, int V, int MW,
-                    int num_tiles, float *gw, int32_t *status, cudaStream_t stream) {
+                    const uint32_t *masks, int64_t M, int V, float *gw, int32_t *status, cudaStream_t stream) {
     const int groups = (V + kWtGroupOffsets - 1) / kWtGroupOffsets;
+    const int num_tiles = (int)((M + kWtTile - 1) / kWtTile);
+    const int MW = (V + 31) / 32;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -465,11 +469,11 @@ int launch_wgrad_tc(int dtype, const void *feats, const void *gout, const int32_
     const int grid = sms;                   // one CTA per SM (all 512 TMEM columns)
     if (dtype == SPCONV_F16)
         wgrad_tc_kernel<__half><<<grid, kWtThreads, kWtSmem, stream>>>(
-            (const __half *)feats, (const __half *)gout, nbr, order, uni, list, cnt, M, V, MW, num_tiles, groups, gw,
+            (const __half *)feats, (const __half *)gout, nbr, order, masks, M, V, MW, num_tiles, groups, gw,
             status, wait_limit_ns());
     else
         wgrad_tc_kernel<__nv_bfloat16><<<grid, kWtThreads, kWtSmem, stream>>>(
-            (const __nv_bfloat16 *)feats, (const __nv_bfloat16 *)gout, nbr, order, uni, list, cnt, M, V, MW, num_tiles,
+            (const __nv_bfloat16 *)feats, (const __nv_bfloat16 *)gout, nbr, order, masks, M, V, MW, num_tiles,
             groups, gw, status, wait_limit_ns());
     return check_launch("wgrad_tc_kernel");
 }
