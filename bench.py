@@ -516,6 +516,10 @@ def main():
         dom_ms = per_stage[dom][0] / per_stage[dom][1]
         achieved = kern_bytes[dom] / (dom_ms / 1e3) / 1e9
         traffic = _traffic_per_launch(f"{args.workload}:{dom}")
+        if traffic is not None and w.num_voxels != w_all.num_voxels:
+            # the capture ran the whole workload; a rank of the batch split launches on its share
+            # (DRAM bytes grow with the voxels a launch processes)
+            traffic = int(round(traffic * w.num_voxels / w_all.num_voxels))
         # Second figure: the conv alone, as when a layer reuses the map (neighbour cache passed
         # back), from the conv kernel's own per-launch events in the eager steps above.
         cached_map = None

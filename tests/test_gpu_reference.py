@@ -40,11 +40,17 @@ def test_reference_cuda_map_equals_library_and_oracle(ref_module, name):
     np.testing.assert_array_equal(oracle.neighbor_map(coords, shape, ks, dil), ref)
 
 
-@pytest.mark.parametrize("name", ["cube", "wide5"])
+@pytest.mark.parametrize("name", ["cube", "lidar", "indoor", "wide3", "wide5", "indoor_shuffled"])
 def test_reference_cuda_map_full_size(ref_module, name):
-    w = gpu_cases.workload(name)
-    ref = _ref_map(ref_module, w.coords, w.shape, w.kernel_size, w.dilation)
+    """Full-size workloads. Their coordinates are sorted, so the 3x3x3 maps take the library's
+    column path; `indoor_shuffled` permutes the indoor rows (seeded), which sends the 2M-voxel
+    build down the hash path instead."""
+    w = gpu_cases.workload(name.replace("_shuffled", ""))
+    coords = w.coords
+    if name.endswith("_shuffled"):
+        coords = np.ascontiguousarray(coords[np.random.default_rng(5).permutation(coords.shape[0])])
+    ref = _ref_map(ref_module, coords, w.shape, w.kernel_size, w.dilation)
     N, _C, W, H, D = w.shape
-    nbr, _, _ = _native.build_neighbor_map(torch.from_numpy(w.coords).cuda(), N, W, H, D,
+    nbr, _, _ = _native.build_neighbor_map(torch.from_numpy(coords).cuda(), N, W, H, D,
                                            w.kernel_size, w.dilation)
     np.testing.assert_array_equal(nbr.cpu().numpy().view(np.uint32), ref)
