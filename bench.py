@@ -123,13 +123,14 @@ def _traffic_per_launch(key: str):
 
 
 def _launches_per_step(M: int, V: int, cells: int) -> int:
-    """Kernels one forward launches: insert, map, order (one bucket scatter, or three per 8-bit
-    radix pass for maps of <= 27-offset kernels of >= 2^19 voxels, or of > 2^17 voxels filling
-    at most 0.3 % of the grid), conv."""
+    """Kernels one forward launches: insert, map, order (one bucket scatter, or, for maps of
+    <= 27-offset kernels of >= 2^19 voxels or of > 2^17 voxels filling at most 0.3 % of the
+    grid, a scan and a scatter per 8-bit radix pass plus a count for every pass after the first,
+    whose counts the map kernel makes), conv."""
     if V <= 27 and (M >= (1 << 19) or ((1 << 17) < M <= 0.003 * cells)):
         drop = max(V - 21, 0)
         passes = (4 + V - 1 - drop + 7) // 8
-        return 2 + 3 * passes + 1
+        return 2 + 3 * passes - 1 + 1
     return 4
 
 

@@ -17,7 +17,8 @@
 //      shapes with a bitmap, map_kernel otherwise): one thread per voxel screens its
 //      offsets against the bitmap, probes the table only for occupied cells, stages the
 //      voxel's map row in shared memory (written out coalesced) and builds its offset mask;
-//      each block adds its voxels' order keys (popcount class, mask hash) to a histogram;
+//      each block adds its voxels' order keys (popcount class, mask hash) to a histogram, or,
+//      when the radix order follows, the low digits of their radix keys to the sort's counts;
 //   4. order: order_kernel scans the histogram in every block and scatters voxel ids by key
 //      (block-aggregated cursor atomics) - or, for maps of >= 2^19 voxels of kernels of
 //      <= 27 offsets, a stable radix sort by (class, mask) (sort_*_kernel).
@@ -187,6 +188,44 @@ __device__ __forceinline__ uint32_t aggregated_inc(uint32_t *counter, uint32_t k
     return base + __popc(lt);
 }
 
+constexpr int kSortCompBits = 20;
+
+__device__ __host__ __forceinline__ int order_key_drop(int V) {
+    return V - 1 > kSortCompBits ? V - 1 - kSortCompBits : 0;
+}
+
+__device__ __forceinline__ uint32_t order_key(uint32_t m, int V) {
+    const int c = V / 2, drop = order_key_drop(V);
+    m &= (1u << V) - 1u;                                        // V <= 27
+    const uint32_t comp = (m & ((1u << c) - 1u)) | ((m >> (c + 1)) << c);
+    const uint32_t pc = (uint32_t)__popc(m);
+    const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+    return (cls << (V - 1 - drop)) | (comp >> drop);
+}
+
+// Order histogram entry of a voxel with offset mask word `m0` (the first), popcount `pc` and
+// mask hash `h`. With sort_nt > 0 (the radix order) the map kernels make the sort's first
+// counts: the low 8-bit digit of the voxel's radix key, counted per 2048-voxel sort tile (every
+// map block lies inside one tile); otherwise the bucket order's (class, hash) bucket.
+__device__ __forceinline__ uint32_t order_bucket(uint32_t m0, uint32_t pc, uint32_t h, int V, int sort_nt) {
+    if (sort_nt > 0) return order_key(m0, V) & 255u;
+    const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
+    return cls * 256u + (h & 255u);
+}
+
+// Adds a block's shared-memory histogram (after a __syncthreads) to the global one: the bucket
+// histogram, or (sort_nt > 0) column tile = i0 / kSortTile of the radix sort's pass-0 digit
+// counts [256][sort_nt], which the workspace clear zeroes.
+__device__ __forceinline__ void order_hist_flush(const uint32_t *s_hist, uint32_t *hist, int sort_nt, int64_t i0) {
+    if (sort_nt > 0) {
+        const int64_t tile = i0 / kSortTile;
+        for (int d = threadIdx.x; d < 256; d += blockDim.x)
+            if (s_hist[d]) atomicAdd(hist + (int64_t)d * sort_nt + tile, s_hist[d]);
+    } else {
+        block_hist_flush(s_hist, hist);
+    }
+}
+
 // ---------------------------------------------------------------------------------------
 // Table: packed 64-bit slots for volumes < 2^32 (key = flat index), or 64-bit keys plus a
 // separate row array otherwise; stored complemented, so 0 = empty. A key hashes to a group
@@ -335,7 +374,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
            int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
            const unsigned long long *__restrict__ table, const uint32_t *__restrict__ vals,
            const uint32_t *__restrict__ bitmap, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr, uint32_t *__restrict__ masks,
-           uint32_t *hist, int32_t *status) {
+           uint32_t *hist, int sort_nt, int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
     extern __shared__ int4 s_off[];                                   // [V] (ox, oy, oz, 0)
     long long *s_delta = reinterpret_cast<long long *>(s_off + V);   // [V] flat-key deltas
@@ -367,7 +406,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     const unsigned long long base = ((((unsigned long long)(long long)c.x * W + c.y) * H + c.z) * D) + c.w;
     const int center = V / 2;
     bool wrapped = false;
-    uint32_t pc = 0, h = 0x9e3779b9u;
+    uint32_t pc = 0, h = 0x9e3779b9u, m0 = 0u;
     for (int vb = 0; vb < V; vb += 32) {
         const int vend = min(vb + 32, V);
         uint32_t bits = 0;
@@ -419,13 +458,13 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             }
         }
         if (valid) masks[i * (int64_t)MW + (vb >> 5)] = bits;
+        if (vb == 0) m0 = bits;
         pc += __popc(bits);
         h = fmix32(h ^ bits);
     }
     if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
     {
-        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-        const uint32_t key = cls * 256u + (h & 255u);
+        const uint32_t key = order_bucket(m0, pc, h, V, sort_nt);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
         if (valid && hist) aggregated_inc(s_hist, key, active);
     }
@@ -443,7 +482,7 @@ map_kernel(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             if (v >= V) { v -= V; ++il; }
         }
     }
-    if (hist) block_hist_flush(s_hist, hist);
+    if (hist) order_hist_flush(s_hist, hist, sort_nt, i0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -463,7 +502,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
               int Kw, int Kh, int Kd, int Dw, int Dh, int Dd, int V, int MW, int vstride,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
-              uint32_t *__restrict__ masks, uint32_t *hist,
+              uint32_t *__restrict__ masks, uint32_t *hist, int sort_nt,
               int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
     extern __shared__ int32_t s_stage[];                       // [blockDim.x][vstride]
@@ -560,8 +599,8 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
     h = fmix32(h ^ cur_bits);
     if (wrapped) raise_status(status, SPCONV_STATUS_TABLE_FULL);
     {
-        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-        const uint32_t k = cls * 256u + (h & 255u);
+        // (the radix order needs V <= 27: cur_bits is then the only mask word)
+        const uint32_t k = order_bucket(cur_bits, pc, h, V, sort_nt);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
         if (valid && hist) aggregated_inc(s_hist, k, active);
     }
@@ -587,7 +626,7 @@ map_kernel_bm(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
             }
         }
     }
-    if (hist) block_hist_flush(s_hist, hist);
+    if (hist) order_hist_flush(s_hist, hist, sort_nt, i0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -606,7 +645,7 @@ __device__ __forceinline__ void
 k3_hash_block(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
-              uint32_t *__restrict__ masks, uint32_t *hist,
+              uint32_t *__restrict__ masks, uint32_t *hist, int sort_nt,
               int32_t *status, const int32_t *dup_flag, uint32_t *s_hist, int32_t *s_stage) {
     constexpr int V = 27;
 
@@ -747,8 +786,7 @@ k3_hash_block(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
     {
         const uint32_t pc = __popc(bits);
         const uint32_t h = fmix32(0x9e3779b9u ^ bits);
-        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t k = order_bucket(bits, pc, h, V, sort_nt);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
         if (valid && hist) aggregated_inc(s_hist, k, active);
     }
@@ -763,7 +801,7 @@ k3_hash_block(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, i
         for (int e = tid; e < n4; e += kMapK3Threads) dst[e] = src[e];
         for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
     }
-    if (hist) block_hist_flush(s_hist, hist);
+    if (hist) order_hist_flush(s_hist, hist, sort_nt, i0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -843,7 +881,7 @@ template <bool DD1>
 __device__ __forceinline__ void
 k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ keys,
                 const int2 *__restrict__ colrange, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
-                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist,
+                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, int sort_nt,
                 uint32_t *s_hist, int32_t *s_stage) {
     constexpr int V = 27;
     const int tid = threadIdx.x;
@@ -981,8 +1019,7 @@ k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ ke
     {
         const uint32_t pc = __popc(bits);
         const uint32_t h = fmix32(0x9e3779b9u ^ bits);
-        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t k = order_bucket(bits, pc, h, V, sort_nt);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
         if (valid && hist) aggregated_inc(s_hist, k, active);
     }
@@ -996,7 +1033,7 @@ k3_sorted_block(const int4 *__restrict__ coords, const uint32_t *__restrict__ ke
         for (int e = tid; e < n4; e += kMapK3Threads) dst[e] = src[e];
         for (int e = (n4 << 2) + tid; e < total; e += kMapK3Threads) out[e] = s_stage[e];
     }
-    if (hist) block_hist_flush(s_hist, hist);
+    if (hist) order_hist_flush(s_hist, hist, sort_nt, i0);
 }
 
 // The 3x3x3 map kernel: the column path when this call's input is strictly increasing (the
@@ -1007,16 +1044,17 @@ __global__ void __launch_bounds__(kMapK3Threads, 4)
 map_kernel_k3(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Dw, int Dh, int Dd,
               const unsigned long long *__restrict__ table, const uint32_t *__restrict__ bitmap,
               int64_t bm_words, uint64_t gmask, uint32_t shift, int32_t *__restrict__ nbr,
-              uint32_t *__restrict__ masks, uint32_t *hist, int32_t *status, const int32_t *dup_flag,
+              uint32_t *__restrict__ masks, uint32_t *hist, int sort_nt, int32_t *status, const int32_t *dup_flag,
               const uint32_t *__restrict__ keys, const int2 *__restrict__ colrange, const int32_t *unsorted) {
     __shared__ uint32_t s_hist[kOrderBuckets];
     __shared__ __align__(16) int32_t s_stage[kMapK3Threads * 27];   // read back as int4
     grid_dependency_wait();                                     // the insert's table / the prep's keys
     if (unsorted && *unsorted == 0)
-        k3_sorted_block<DD1>(coords, keys, colrange, M, W, H, D, Dw, Dh, Dd, nbr, masks, hist, s_hist, s_stage);
+        k3_sorted_block<DD1>(coords, keys, colrange, M, W, H, D, Dw, Dh, Dd, nbr, masks, hist, sort_nt, s_hist,
+                             s_stage);
     else
         k3_hash_block<BITMAP>(coords, M, W, H, D, Dw, Dh, Dd, table, bitmap, bm_words, gmask, shift, nbr, masks,
-                              hist, status, dup_flag, s_hist, s_stage);
+                              hist, sort_nt, status, dup_flag, s_hist, s_stage);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1063,7 +1101,8 @@ __global__ void __launch_bounds__(kMapColsThreads, kMapColsMinBlocks)
 map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D, int Kw, int Kh, int Kd,
                 int Dw, int Dh, int Dd, int V, int MW, const unsigned long long *__restrict__ table,
                 const uint32_t *__restrict__ bitmap, int64_t bm_words, uint64_t gmask, uint32_t shift,
-                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, int32_t *status) {
+                int32_t *__restrict__ nbr, uint32_t *__restrict__ masks, uint32_t *hist, int sort_nt,
+                int32_t *status) {
     __shared__ uint32_t s_hist[kOrderBuckets];
     // 32 offset columns of every row of the block; stride 33 keeps both the per-thread
     // row writes and the per-warp row-segment reads free of bank conflicts.
@@ -1229,13 +1268,12 @@ map_kernel_cols(const int4 *__restrict__ coords, int64_t M, int W, int H, int D,
                 h = fmix32(h ^ bits[w]);
             }
         }
-        const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-        const uint32_t k = cls * 256u + (h & 255u);
+        const uint32_t k = order_bucket(bits[0], pc, h, V, sort_nt);
         const uint32_t active = __ballot_sync(0xffffffffu, valid);
         if (valid && hist) aggregated_inc(s_hist, k, active);
     }
     __syncthreads();
-    if (hist) block_hist_flush(s_hist, hist);
+    if (hist) order_hist_flush(s_hist, hist, sort_nt, i0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1319,27 +1357,14 @@ order_kernel(const uint32_t *__restrict__ masks, int64_t M, int MW, const uint32
 //     share their high offsets, so a 128-voxel tile of the order needs few offsets beyond its
 //     voxels' own. Equal keys keep input order (the (b,x,y,z) order of the coordinates), so
 //     their feature rows are gathered with spatial locality.
-//     Per 8-bit digit pass: sort_count_kernel counts each 2048-key tile's digits,
+//     Per 8-bit digit pass: the tile digit counts (made for the first pass by the map kernels,
+//     which add each block's low key digits to its tile's column, and for later passes by
+//     sort_count_kernel),
 //     sort_scan_kernel (one block per digit) scans the counts over tiles, and
 //     sort_scatter_kernel ranks each tile's keys stably (lanes with equal digits found by
 //     eight ballots, per-warp digit counters, warps in input order) and writes them to their
 //     sorted positions.
 // ---------------------------------------------------------------------------------------
-constexpr int kSortCompBits = 20;
-
-__device__ __host__ __forceinline__ int order_key_drop(int V) {
-    return V - 1 > kSortCompBits ? V - 1 - kSortCompBits : 0;
-}
-
-__device__ __forceinline__ uint32_t order_key(uint32_t m, int V) {
-    const int c = V / 2, drop = order_key_drop(V);
-    m &= (1u << V) - 1u;                                        // V <= 27
-    const uint32_t comp = (m & ((1u << c) - 1u)) | ((m >> (c + 1)) << c);
-    const uint32_t pc = (uint32_t)__popc(m);
-    const uint32_t cls = pc == 0 ? 0u : min(pc - 1u, 15u);
-    return (cls << (V - 1 - drop)) | (comp >> drop);
-}
-
 // Number of 8-bit passes for the keys of a V-offset kernel.
 static int sort_passes(int V) {
     return (4 + V - 1 - order_key_drop(V) + 7) / 8;
@@ -1357,10 +1382,11 @@ __device__ __forceinline__ uint32_t digit_peers(uint32_t d, uint32_t active) {
     return peers;
 }
 
-template <bool FIRST>
+// Digit counts of each 2048-key tile for passes after the first (the map kernels count the
+// first pass's digits as they build the masks).
 __global__ void __launch_bounds__(kSortThreads)
-sort_count_kernel(const uint32_t *__restrict__ masks, int V, const uint32_t *__restrict__ keys,
-                  int64_t M, int ntiles, int shift, uint32_t *__restrict__ counts) {
+sort_count_kernel(const uint32_t *__restrict__ keys, int64_t M, int ntiles, int shift,
+                  uint32_t *__restrict__ counts) {
     __shared__ uint32_t s_cnt[256];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid < 256) s_cnt[tid] = 0u;
@@ -1373,7 +1399,7 @@ sort_count_kernel(const uint32_t *__restrict__ masks, int V, const uint32_t *__r
     for (int k = 0; k < kSortWarpItems / 32; ++k) {
         const int64_t e = e0 + 32 * k;
         d[k] = 0xffffffffu;
-        if (e < M) d[k] = ((FIRST ? order_key(__ldg(masks + e), V) : __ldg(keys + e)) >> shift) & 255u;
+        if (e < M) d[k] = (__ldg(keys + e) >> shift) & 255u;
     }
 #pragma unroll
     for (int k = 0; k < kSortWarpItems / 32; ++k) {
@@ -1577,7 +1603,10 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
     // Stable radix-sort order for kernels of <= kSortMaxV offsets when the workspace has room
     // (radix_order); the map kernels then skip the bucket histogram.
     const bool radix = L.sort_tiles > 0 && V <= kSortMaxV;
-    if (radix) hist = nullptr;
+    // The radix order's first digit counts come from the map kernels themselves (into the sort
+    // counts, zeroed with the workspace), so its first pass needs no counting launch.
+    const int sort_nt = radix ? L.sort_tiles : 0;
+    if (radix) hist = (uint32_t *)(ws + L.sort_counts);
 
     int32_t *unsorted = L.cols ? dup_flag + 1 : nullptr;       // per-call word: the hash path runs
     uint32_t *keys = L.cols ? (uint32_t *)(ws + L.keys) : nullptr;
@@ -1633,7 +1662,7 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
         launch_pdl(k3_fn, dim3(grid), dim3(kMapK3Threads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Dw, Dh, Dd, (const unsigned long long *)table,
                    (const uint32_t *)bitmap, L.bitmap_words, gmask, shift, neighbor_map, masks, hist,
-                   status, (const int32_t *)dup_flag, (const uint32_t *)keys,
+                   sort_nt, status, (const int32_t *)dup_flag, (const uint32_t *)keys,
                    (const int2 *)(L.cols ? ws + L.colrange : nullptr), (const int32_t *)unsorted);
     } else if (!key64 && bitmap && V <= kMapColsMaxV && (Kd - 1) * Dd + 1 <= 32) {
         const int grid = (int)((M + kMapColsThreads - 1) / kMapColsThreads);
@@ -1641,7 +1670,7 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
         launch_pdl(map_kernel_cols, dim3(grid), dim3(kMapColsThreads), 0, stream,
                    (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW,
                    (const unsigned long long *)table, (const uint32_t *)bitmap, L.bitmap_words, gmask,
-                   shift, neighbor_map, masks, hist, status);
+                   shift, neighbor_map, masks, hist, sort_nt, status);
     } else if (bitmap && Kd <= kColBatchMax) {
         // 256 voxels per block while their staged rows fit in 64 KB, else 128.
         const int nthr = ((size_t)kMapBmMaxThreads * (V | 1) * 4 <= 64 * 1024) ? kMapBmMaxThreads : 128;
@@ -1654,7 +1683,7 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         bm_fn<<<grid, nthr, smem, stream>>>(
             (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, bitmap,
-            L.bitmap_words, gmask, shift, neighbor_map, masks, hist, status);
+            L.bitmap_words, gmask, shift, neighbor_map, masks, hist, sort_nt, status);
     } else {
         const int map_grid = (int)((M + kMapThreads - 1) / kMapThreads);
         // Rows are staged in shared memory (odd row stride: conflict-free) unless V is so
@@ -1668,7 +1697,7 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
         stage_mark(SPCONV_STAGE_MAP, 0, stream);
         map_fn<<<map_grid, kMapThreads, map_smem, stream>>>(
             (const int4 *)coords, M, W, H, D, Kw, Kh, Kd, Dw, Dh, Dd, V, MW, vstride, table, vals, bitmap,
-            gmask, shift, neighbor_map, masks, hist, status);
+            gmask, shift, neighbor_map, masks, hist, sort_nt, status);
     }
     if (int rc = check_launch("map_kernel")) return rc;
     stage_mark(SPCONV_STAGE_MAP, 1, stream);
@@ -1685,9 +1714,10 @@ static int build_map(const int32_t *coords, int64_t M, int batch, int W, int H, 
             const bool first = p == 0, last = p + 1 == passes;
             uint32_t *ko = kb[p & 1], *vo = last ? (uint32_t *)order : vb[p & 1];
             const uint32_t *ki = first ? nullptr : kb[(p + 1) & 1], *vi = first ? nullptr : vb[(p + 1) & 1];
-            launch_pdl(first ? sort_count_kernel<true> : sort_count_kernel<false>, dim3(nt), dim3(kSortThreads),
-                       0, stream, (const uint32_t *)masks, V, ki, M, nt, 8 * p, cp);
-            if (int rc = check_launch("sort_count_kernel")) return rc;
+            if (!first) {                    // the first pass's counts come from the map kernel
+                launch_pdl(sort_count_kernel, dim3(nt), dim3(kSortThreads), 0, stream, ki, M, nt, 8 * p, cp);
+                if (int rc = check_launch("sort_count_kernel")) return rc;
+            }
             launch_pdl(sort_scan_kernel, dim3(256), dim3(kSortThreads), 0, stream, cp, nt, tp);
             if (int rc = check_launch("sort_scan_kernel")) return rc;
             auto fn = first ? (last ? sort_scatter_kernel<true, true> : sort_scatter_kernel<true, false>)
