@@ -122,16 +122,22 @@ def _traffic_per_launch(key: str):
     return None
 
 
-def _launches_per_step(M: int, V: int, cells: int) -> int:
-    """Kernels one forward launches: insert, map, order (one bucket scatter, or, for maps of
-    <= 27-offset kernels of >= 2^19 voxels or of > 2^17 voxels filling at most 0.3 % of the
-    grid, a scan and a scatter per 8-bit radix pass plus a count for every pass after the first,
-    whose counts the map kernel makes), conv."""
+def _launches_per_step(M: int, kernel, shape) -> int:
+    """Kernels one forward launches: for 3x3x3 kernels on grids of < 2^32 cells and <= 2^23
+    (b, x, y) columns the sorted-input prep and the conditional table clear; insert, map, order
+    (one bucket scatter, or, for maps of <= 27-offset kernels of >= 2^19 voxels or of > 2^17
+    voxels filling at most 0.3 % of the grid, a scan and a scatter per 8-bit radix pass plus a
+    count for every pass after the first, whose counts the map kernel makes), conv. Workspace
+    clears are driver memsets, not counted."""
+    V = int(np.prod(kernel))
+    N, W, H, D = int(shape[0]), int(shape[2]), int(shape[3]), int(shape[4])
+    cells = N * W * H * D
+    prep = 2 if tuple(kernel) == (3, 3, 3) and cells < (1 << 32) and N * W * H <= (1 << 23) else 0
     if V <= 27 and (M >= (1 << 19) or ((1 << 17) < M <= 0.003 * cells)):
         drop = max(V - 21, 0)
         passes = (4 + V - 1 - drop + 7) // 8
-        return 2 + 3 * passes - 1 + 1
-    return 4
+        return prep + 2 + 3 * passes - 1 + 1
+    return prep + 4
 
 
 def _dist():
@@ -553,8 +559,7 @@ def main():
                     "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()), "steps": KE,
                     "pipelined": f"{NS} CUDA streams: step i+1's H2D overlaps step i's op and D2H",
                     "serial_value": e2e_serial},
-            "gpu_launches": _launches_per_step(w.num_voxels, int(np.prod(w.kernel_size)),
-                                               int(w.shape[0]) * int(np.prod(w.shape[2:]))) * K,
+            "gpu_launches": _launches_per_step(w.num_voxels, w.kernel_size, w.shape) * K,
             "clocks": clk,
         }
         if train is not None:
